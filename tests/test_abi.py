@@ -1,0 +1,51 @@
+"""The C-ABI library loads and exports every entry point include/xpager.h declares.
+
+No GPU needed: only symbol lookup and host-side argument checks.
+"""
+
+import ctypes
+import os
+import re
+
+from vllm_expert_pager import native
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include",
+                      "xpager.h")
+
+
+def declared() -> list[str]:
+    text = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    return [m.group(1) for m in
+            re.finditer(r"^(?:const\s+)?[a-z_0-9]+\s*\*?\s*([a-z_0-9]+)\s*\(", text, flags=re.M)]
+
+
+def test_header_declares_entry_points():
+    names = declared()
+    assert "xp_gather_rows" in names and "ssd_start" in names and len(names) >= 20
+
+
+def test_library_exports_every_declared_symbol():
+    so = ctypes.CDLL(native.LIB_PATH)
+    for name in declared():
+        assert hasattr(so, name), name
+
+
+def test_bindings_cover_the_header():
+    assert sorted(declared()) == sorted(native._SIGNATURES)
+
+
+def test_status_strings_and_version():
+    lib = native.lib()
+    assert lib.xp_version() >= 1
+    assert b"invalid" in lib.xp_status_string(native.XP_EINVAL)
+    assert b"pitch" in lib.xp_status_string(native.XP_EPITCH)
+
+
+def test_device_calls_reject_bad_arguments_before_launching():
+    # Argument checks run on the host and return before any CUDA call.
+    lib = native.lib()
+    assert lib.xp_acquire(None, 3, 1, 16, None, None, None, None, 4, None, None, None,
+                          None) == native.XP_EINVAL
+    assert lib.xp_decode_rows(None, 1, None, None, None, None, 0, None, 0, None, 0, None, 0,
+                              None, 7, None) == native.XP_EINVAL
+    assert lib.xp_fetch_wait(None, 1, None, None, None, 256, 4, 1, 1, None) == native.XP_EINVAL

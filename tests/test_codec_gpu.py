@@ -1,0 +1,116 @@
+"""GPU decoder (decode.cu, via the C ABI) against the reference's records and the CPU oracle.
+
+Bit-exact: the expanded slot bytes equal the raw fp8 rows.
+"""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import _lib as oracle_lib
+from oracle import codec as oc
+from rowgen import rows
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+DEV = torch.device("cuda")
+
+
+def decode_one(rec: np.ndarray, lut: np.ndarray, n: int, chunk: int, rec1=None, lut1=None,
+               n1=None) -> list[np.ndarray]:
+    """Decode one expert (names 0 and 1) through decode_rows; name 1 defaults to name 0."""
+    from vllm_expert_pager import codec
+
+    rec1 = rec if rec1 is None else rec1
+    lut1 = lut if lut1 is None else lut1
+    n1 = n if n1 is None else n1
+    stg = [torch.from_numpy(r.copy()).to(DEV).view(1, -1) for r in (rec, rec1)]
+    dst = [torch.zeros((1, m), dtype=torch.uint8, device=DEV) for m in (n, n1)]
+    luts = torch.from_numpy(np.stack([lut, lut1])[None]).to(DEV)
+    todo = torch.zeros((1,), dtype=torch.int64, device=DEV)
+    dst_row = torch.zeros((1,), dtype=torch.int64, device=DEV)
+    cache_row = torch.full((1,), -1, dtype=torch.int64, device=DEV)
+    codec.decode_rows(todo, dst_row, cache_row, stg, dst, luts, chunk=chunk)
+    torch.cuda.synchronize()
+    return [d[0].cpu().numpy() for d in dst]
+
+
+@pytest.mark.parametrize("chunk", [64, 512])
+@pytest.mark.parametrize("i", range(4), ids=["realistic", "uniform", "geometric", "constant"])
+def test_decodes_reference_records(chunk, i):
+    g = np.load(os.path.join(GOLDEN, "codec.npz"))
+    raw, rec, lut = g[f"c{chunk}_{i}_raw"], g[f"c{chunk}_{i}_rec"], g[f"c{chunk}_{i}_lut"]
+    a, b = decode_one(rec, lut, raw.size, chunk)
+    assert np.array_equal(a, raw) and np.array_equal(b, raw)
+
+
+def test_decodes_config1_experts():
+    """Config 1: 8 full-size experts (w13 2 MiB + w2 1 MiB) round-trip byte for byte."""
+    from vllm_expert_pager import codec, synthetic
+
+    for ex in synthetic.fp8_experts(8, seed=0):
+        raws = [synthetic.row_bytes(ex[name][0]).numpy() for name in synthetic.SHAPES]
+        encs = [codec.encode(torch.from_numpy(r), codec.pitch_of(r.size, 0.89, 4096)) for r in raws]
+        got = decode_one(encs[0][0].numpy(), encs[0][1].numpy(), raws[0].size, 512,
+                         encs[1][0].numpy(), encs[1][1].numpy(), raws[1].size)
+        assert np.array_equal(got[0], raws[0]) and np.array_equal(got[1], raws[1])
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_random_distributions_match_oracle(seed):
+    """Skewed, flat and degenerate exponent histograms at several chunk sizes."""
+    rng = np.random.default_rng(seed)
+    chunk = [8, 16, 64, 512, 128, 32][seed]
+    n = 32 * chunk * int(rng.integers(1, 5))
+    p = rng.dirichlet(np.full(16, [0.05, 0.3, 1.0, 5.0, 0.1, 2.0][seed]))
+    raw = rows(100 + seed, n, p.tolist()).numpy()
+    rec, lut, _ = oc.encode(raw, oc.pitch_of(n, 1.5, 4096) + 4096, chunk)
+    a, _ = decode_one(rec, lut, n, chunk)
+    assert np.array_equal(a, oracle_lib.decode(rec, lut, n, chunk))
+    assert np.array_equal(a, raw)
+
+
+def test_decode_rows_follows_todo_and_skips():
+    """The reference test_codec.py::test_decode_rows_follows_todo_and_skips, at CHUNK=64."""
+    from vllm_expert_pager import codec
+
+    CHUNK, E = 64, 8
+    N = 2 * CHUNK * 32
+    ns = (N, N // 2)
+    pitches = [codec.pitch_of(n, 1.25, 4096) for n in ns]
+    raws = {e: [rows(10 * e + k, n) for k, n in enumerate(ns)] for e in (3, 5, 6)}
+    staging = [torch.zeros((3, p), dtype=torch.uint8, device=DEV) for p in pitches]
+    lut = torch.zeros((E, 2, codec.LUT_BYTES), dtype=torch.uint8, device=DEV)
+    for j, e in enumerate((3, 5, 6)):
+        for k in range(2):
+            staging[k][j], lut[e, k] = codec.encode(raws[e][k].to(DEV), pitches[k], CHUNK)
+    dst = [torch.zeros((2, n), dtype=torch.uint8, device=DEV) for n in ns]
+    todo = torch.tensor([3, 5, 6], dtype=torch.int64, device=DEV)
+    dst_row = torch.zeros((E,), dtype=torch.int64, device=DEV)
+    dst_row[3], dst_row[5], dst_row[6] = 1, 0, 0
+    cache_row = torch.full((E,), -1, dtype=torch.int64, device=DEV)
+    cache_row[5] = 2
+    skip = torch.tensor([6, -1, -1], dtype=torch.int64, device=DEV)
+    codec.decode_rows(todo, dst_row, cache_row, staging, dst, lut, skip=skip, chunk=CHUNK)
+    torch.cuda.synchronize()
+    for k in range(2):
+        assert torch.equal(dst[k][1].cpu(), raws[3][k])
+        assert not dst[k][0].any()
+    codec.decode_rows(todo, dst_row, cache_row, staging, dst, lut, chunk=CHUNK)
+    torch.cuda.synchronize()
+    for k in range(2):
+        assert torch.equal(dst[k][0].cpu(), raws[6][k])
+
+
+def test_decode_rejects_bad_shapes():
+    from vllm_expert_pager import codec
+
+    t = torch.zeros((1,), dtype=torch.int64, device=DEV)
+    stg = [torch.zeros((1, 4096), dtype=torch.uint8, device=DEV)] * 2
+    dst = [torch.zeros((1, 1000), dtype=torch.uint8, device=DEV)] * 2  # not a multiple of 32*chunk
+    lut = torch.zeros((1, 2, 512), dtype=torch.uint8, device=DEV)
+    with pytest.raises(ValueError):
+        codec.decode_rows(t, t, t, stg, dst, lut, chunk=64)

@@ -60,15 +60,9 @@ def test_encode_rejects_rows_over_pitch(g):
 
 def test_over_pitch_message_matches_reference(g):
     # the reference message for the test_codec.py rows(3) case at CHUNK=64
-    import torch
+    from rowgen import rows
 
-    gen = torch.Generator().manual_seed(3)
-    p = [0.0] * 4 + [0.001, 0.002, 0.004, 0.008, 0.016, 0.032, 0.064, 0.125, 0.228, 0.315,
-                     0.188, 0.015]
-    exp = torch.multinomial(torch.tensor(p, dtype=torch.float64), 4096, replacement=True,
-                            generator=gen)
-    sm = torch.randint(0, 256, (4096,), dtype=torch.uint8, generator=gen) & 0x87
-    raw = (sm | (exp.to(torch.uint8) << 3)).numpy()
+    raw = rows(3, 4096).numpy()
     with pytest.raises(ValueError) as e:
         oc.encode(raw, 1024, 64)
     assert str(e.value) == str(g["over_pitch_msg"])

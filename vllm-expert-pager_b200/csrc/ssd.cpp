@@ -1,0 +1,274 @@
+// Host server of the SSD tier: serves the GPU's read requests from the paging
+// file into pinned RAM-tier rows.
+//
+// Keeps the C ABI and protocol of monochromegane/vllm-expert-pager
+// src/vllm_expert_pager/store.py:68-309 (bound by ctypes at store.py:312-331):
+//  * req = [re-publishes, give-ups] + ring slots of [seq, layer, expert[B], row[B]];
+//    the GPU publishes seq last with release semantics (gather.cu);
+//  * requests are served in seq order; done = seq is stored with release
+//    semantics once every read of the request finished, even if one failed;
+//  * a read is one preadv of record_bytes at (layer*E + e)*record_bytes into
+//    the row's pinned pieces (one per name), with bounds checks;
+//  * while idle the server rewrites done when the GPU's re-publish counter
+//    moves or after 2^25 idle spins (a lost done), counts seq gaps as missed,
+//    and honours a test-only delay.
+//
+// Implementation: one server thread spinning on the ring (a sleep adds ~100 us
+// to the round trip) and a pool of worker threads that take the request's jobs
+// one at a time under a mutex (a job is a multi-megabyte read).
+#define _GNU_SOURCE 1
+#include <errno.h>
+#include <sched.h>
+#include <stdarg.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string.h>
+#include <sys/uio.h>
+#include <time.h>
+#include <unistd.h>
+
+#include <atomic>
+#include <condition_variable>
+#include <mutex>
+#include <thread>
+#include <vector>
+
+#include "xpager.h"
+
+namespace {
+
+constexpr int kMaxNames = 4;
+constexpr long kHead = 2;
+
+double now_s() {
+  timespec t;
+  clock_gettime(CLOCK_MONOTONIC, &t);
+  return static_cast<double>(t.tv_sec) + 1e-9 * static_cast<double>(t.tv_nsec);
+}
+
+inline void cpu_relax(long &spins) {
+  if (++spins > 200000) {
+    sched_yield();
+    spins = 0;
+  } else {
+#if defined(__x86_64__) || defined(__i386__)
+    __builtin_ia32_pause();
+#elif defined(__aarch64__)
+    asm volatile("yield");
+#endif
+  }
+}
+
+int64_t load_acq(const volatile int64_t *p) { return __atomic_load_n(p, __ATOMIC_ACQUIRE); }
+void store_rel(volatile int64_t *p, int64_t v) { __atomic_store_n(p, v, __ATOMIC_RELEASE); }
+
+struct Server {
+  int fd;
+  volatile int64_t *req, *done;
+  long ring, block, slot_words, L, E, rows, record_bytes;
+  int names;
+  uint8_t *pinned[kMaxNames];
+  long pitch[kMaxNames];
+
+  // statistics (written by the server thread)
+  std::atomic<long> fetches{0}, reads{0}, missed{0};
+  std::atomic<double> io_seconds{0.0};
+  char err[512];
+  std::atomic<int> failing{0}, failed{0};
+  std::atomic<double> test_delay{0.0};
+
+  // the current request's jobs
+  long layer = 0;
+  std::vector<long> job_expert, job_row;
+  // Taking a job and counting it finished happen under mu, so a worker that
+  // wakes up late cannot pair an index of one request with another's count.
+  long njobs = 0, next = 0;
+  std::atomic<long> finished{0};
+  std::mutex mu;
+  std::condition_variable cv;
+  long gen = 0;
+  std::atomic<bool> stop{false};
+  std::vector<std::thread> workers;
+  std::thread server;
+
+  void fail(const char *fmt, ...) {
+    int expected = 0;
+    if (!failing.compare_exchange_strong(expected, 1)) return;  // keep the first failure
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(err, sizeof err, fmt, ap);
+    va_end(ap);
+    failed.store(1, std::memory_order_release);
+  }
+
+  void read_one(long j) {
+    const long e = job_expert[j], row = job_row[j];
+    if (layer < 0 || layer >= L || e < 0 || e >= E) {
+      fail("expert %ld of layer %ld is out of range", e, layer);
+      return;
+    }
+    if (row < 0 || row >= rows) {
+      fail("row %ld for expert %ld of layer %ld is outside the RAM tier of %ld rows", row, e,
+           layer, rows);
+      return;
+    }
+    iovec iov[kMaxNames];
+    for (int i = 0; i < names; ++i) {
+      iov[i].iov_base = pinned[i] + row * pitch[i];
+      iov[i].iov_len = static_cast<size_t>(pitch[i]);
+    }
+    const off_t off = static_cast<off_t>(layer * E + e) * record_bytes;
+    ssize_t n = preadv(fd, iov, names, off);
+    if (n < 0)
+      fail("preadv of expert %ld of layer %ld failed: %s", e, layer, strerror(errno));
+    else if (n != record_bytes)
+      fail("short read: %zd of %ld B for expert %ld of layer %ld", n, record_bytes, e, layer);
+  }
+
+  void run_jobs() {
+    for (;;) {
+      long j;
+      {
+        std::lock_guard<std::mutex> lk(mu);
+        j = next < njobs ? next++ : -1;
+      }
+      if (j < 0) return;
+      read_one(j);
+      std::lock_guard<std::mutex> lk(mu);
+      finished.fetch_add(1, std::memory_order_release);
+    }
+  }
+
+  void worker_main() {
+    long seen = 0;
+    for (;;) {
+      {
+        std::unique_lock<std::mutex> lk(mu);
+        cv.wait(lk, [&] { return gen != seen || stop.load(); });
+        if (stop.load()) return;
+        seen = gen;
+      }
+      run_jobs();
+    }
+  }
+
+  void server_main() {
+    int64_t last = 0, retries = 0;
+    for (;;) {
+      volatile int64_t *slot = req + kHead + ((last + 1) % ring) * slot_words;
+      long spins = 0, idle = 0;
+      int64_t seq;
+      while ((seq = load_acq(slot)) <= last) {
+        if (stop.load(std::memory_order_acquire)) return;
+        // The GPU may not have seen done: rewrite it when the re-publish count
+        // moves, or after a long idle period (store.py:200-207).
+        int64_t r = load_acq(&req[0]);
+        if (r != retries || ++idle > (1L << 25)) {
+          retries = r;
+          idle = 0;
+          store_rel(done, last);
+        }
+        cpu_relax(spins);
+      }
+      const double t0 = now_s();
+      // Requests skipped over were given up by the GPU before they arrived.
+      if (seq > last + 1) missed.fetch_add(static_cast<long>(seq - last - 1));
+      while (test_delay.load() > 0 && now_s() - t0 < test_delay.load()) {
+        if (stop.load(std::memory_order_acquire)) return;
+        usleep(1000);
+      }
+      long n = 0;
+      {
+        std::lock_guard<std::mutex> lk(mu);
+        layer = static_cast<long>(slot[1]);
+        for (long j = 0; j < block; ++j) {
+          int64_t e = slot[2 + j];
+          if (e < 0) continue;
+          job_expert[n] = static_cast<long>(e);
+          job_row[n] = static_cast<long>(slot[2 + block + j]);
+          ++n;
+        }
+        njobs = n;
+        next = 0;
+        finished.store(0, std::memory_order_release);
+        if (n > 1 && !workers.empty()) {  // a single job is read here without waking anyone
+          ++gen;
+          cv.notify_all();
+        }
+      }
+      run_jobs();
+      spins = 0;
+      while (finished.load(std::memory_order_acquire) < n) cpu_relax(spins);
+      fetches.fetch_add(1);
+      reads.fetch_add(n);
+      io_seconds.store(io_seconds.load() + (now_s() - t0));
+      // Re-publishes during a long read are not lost handoffs.
+      retries = load_acq(&req[0]);
+      store_rel(done, seq);
+      last = seq;
+    }
+  }
+};
+
+}  // namespace
+
+extern "C" void *ssd_start(int fd, void *req, void *done, long ring, long block, long L, long E,
+                           long rows, long record_bytes, int names, void **pinned, long *pitch,
+                           int nworkers) {
+  if (names < 1 || names > kMaxNames || !req || !done || ring < 1 || block < 1 || nworkers < 0)
+    return nullptr;
+  Server *s = new (std::nothrow) Server();
+  if (!s) return nullptr;
+  s->fd = fd;
+  s->req = static_cast<volatile int64_t *>(req);
+  s->done = static_cast<volatile int64_t *>(done);
+  s->ring = ring;
+  s->block = block;
+  s->slot_words = 2 + 2 * block;
+  s->L = L;
+  s->E = E;
+  s->rows = rows;
+  s->record_bytes = record_bytes;
+  s->names = names;
+  for (int i = 0; i < names; ++i) {
+    s->pinned[i] = static_cast<uint8_t *>(pinned[i]);
+    s->pitch[i] = pitch[i];
+  }
+  s->err[0] = 0;
+  s->job_expert.assign(static_cast<size_t>(block), 0);
+  s->job_row.assign(static_cast<size_t>(block), 0);
+  for (int i = 0; i < nworkers; ++i) s->workers.emplace_back([s] { s->worker_main(); });
+  s->server = std::thread([s] { s->server_main(); });
+  return s;
+}
+
+extern "C" void ssd_stop(void *server) {
+  Server *s = static_cast<Server *>(server);
+  if (!s) return;
+  {
+    std::lock_guard<std::mutex> lk(s->mu);
+    s->stop.store(true);
+    s->cv.notify_all();
+  }
+  s->server.join();
+  for (auto &t : s->workers) t.join();
+  delete s;
+}
+
+extern "C" void ssd_stats(void *server, long *fetches, long *reads, double *io_seconds,
+                          long *missed) {
+  Server *s = static_cast<Server *>(server);
+  *fetches = s->fetches.load();
+  *reads = s->reads.load();
+  *io_seconds = s->io_seconds.load();
+  *missed = s->missed.load();
+}
+
+extern "C" const char *ssd_error(void *server) {
+  Server *s = static_cast<Server *>(server);
+  return s->failed.load(std::memory_order_acquire) ? s->err : nullptr;
+}
+
+extern "C" void ssd_test_delay(void *server, double seconds) {
+  static_cast<Server *>(server)->test_delay.store(seconds);
+}

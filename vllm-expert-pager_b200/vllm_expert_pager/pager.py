@@ -1,0 +1,237 @@
+"""Per-layer expert paging: the decode path and the chunked working-slab path.
+
+This is the paging half of ``ExpertPagerRoutedExperts`` in
+monochromegane/vllm-expert-pager (src/vllm_expert_pager/experts.py), without
+vLLM: ``experts.py`` of this package owns a ``LayerPager`` per MoE layer and
+only adds the vLLM hooks around it, and the benchmark drives it directly.
+
+* Decode (``topk_ids.numel() <= cache_slots``, experts.py:380-453): one
+  acquire launch updates the VRAM and RAM tables; one gather launch copies the
+  RAM-resident misses (pinned host memory -> slab, or -> staging when
+  compressed) while its last CTA asks the host for the SSD misses and waits;
+  a decode launch expands the staged rows; a second gather (+ decode) copies the
+  rows the host just read.  The MoE then runs on the cache slab with
+  ``expert_map``.
+* Working (``numel() > cache_slots``, experts.py:455-577): the RAM table
+  acquires or is seeded, ``plan_chunks`` lays the needed experts out in N
+  chunks of W rows, and each chunk is copied into a working slab and run
+  through the MoE, whose per-expert contributions are summed once at the end.
+  Chunk k+1's copies run on a side stream into the other half of a 2W-row
+  working slab while chunk k's MoE runs (the reference runs them one after
+  another on one stream); events order each half's copy before its MoE and
+  the MoE before the half is overwritten.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from vllm_expert_pager import codec
+from vllm_expert_pager.acquire import AcquirePair
+from vllm_expert_pager.gather import (
+    as_rows,
+    fetch_publish_rows,
+    fetch_wait_rows,
+    gather_rows,
+)
+from vllm_expert_pager.store import Store
+from vllm_expert_pager.table import ExpertTable
+
+# Expert weights paged through the slabs, in the gather's name order.
+PARAMS = ("w13_weight", "w2_weight")
+
+
+class WorkingSlab:
+    """The working rows shared by every layer (experts.py:79-83,290-318).
+
+    ``halves`` halves of W rows each (2 for the overlapped chunk loop): chunk k
+    uses half k % halves.  Holds weights and scales in slot order, plus the
+    staging for compressed prefill rows (W rows x pitch per half).
+    """
+
+    def __init__(self, rows: int, shapes: dict[str, tuple[tuple[int, ...], torch.dtype]],
+                 store: Store, device: torch.device, halves: int = 2) -> None:
+        self.rows, self.halves = rows, halves
+        self.slab = {
+            name: torch.empty((halves * rows, *shape), dtype=dtype, device=device)
+            for name, (shape, dtype) in shapes.items()
+        }
+        self.staging = None
+        if store.compress:
+            self.staging = [
+                torch.empty((halves * rows, store.pitch[n]), dtype=torch.uint8, device=device)
+                for n in PARAMS
+            ]
+
+    def half(self, h: int) -> dict[str, torch.Tensor]:
+        W = self.rows
+        return {n: t[h * W : (h + 1) * W] for n, t in self.slab.items()}
+
+
+@dataclass
+class DecodeResult:
+    slabs: dict[str, torch.Tensor]
+    expert_map: torch.Tensor
+
+
+class LayerPager:
+    """Tables, slabs and paging launches of one MoE layer."""
+
+    def __init__(self, store: Store, layer: int, cache_slots: int,
+                 scales: dict[str, torch.Tensor], weight_shapes: dict[str, tuple],
+                 working: WorkingSlab) -> None:
+        self.store, self.layer = store, layer
+        E, R, S = store.num_experts, store.ram_slots, cache_slots
+        device = store.device
+        self.num_experts, self.cache_slots = E, S
+        self.vram = ExpertTable(E, S, device)
+        self.ram = ExpertTable(E, R, device)
+        # Warm start: expert e < R was written to RAM-tier slot e (experts.py:256-259).
+        self.ram.slot_of[:R] = self.ram.experts[:R]
+        self.ram.expert_in[:R] = self.ram.experts[:R]
+        self.acquire = AcquirePair(self.vram, self.ram)
+        self.expert_map = self.acquire.expert_map
+        self.scale_names = list(scales)
+        self.cache_slab = {
+            name: torch.empty((S, *shape), dtype=dtype, device=device)
+            for name, (shape, dtype) in weight_shapes.items()
+        }
+        for name, s in scales.items():
+            self.cache_slab[name] = torch.empty((S, *s.shape[1:]), dtype=s.dtype, device=device)
+        self.working = working
+        order = list(PARAMS) + self.scale_names
+        self.cache_rows = [as_rows(self.cache_slab[n]) for n in order]
+        self.scale_rows = [as_rows(scales[n]) for n in self.scale_names]
+        self.cache_bytes = [self.cache_slab[n].view(torch.uint8).reshape(S, -1) for n in PARAMS]
+        self.working_rows = [[as_rows(working.half(h)[n]) for n in order]
+                             for h in range(working.halves)]
+        self.working_bytes = [[working.half(h)[n].view(torch.uint8).reshape(working.rows, -1)
+                               for n in PARAMS] for h in range(working.halves)]
+        # In decode the working slab is idle, so its head stages compressed rows
+        # (S rows x pitch; experts.py:338-353).
+        self.decode_staging = None
+        if store.compress:
+            flat = {n: working.slab[n].view(torch.uint8).reshape(-1) for n in PARAMS}
+            need = {n: S * store.pitch[n] for n in PARAMS}
+            if any(need[n] > flat[n].numel() for n in PARAMS):
+                raise ValueError(
+                    "VLLM_EXPERT_PAGER_WORKING_ROWS cannot hold the decode staging of "
+                    f"{S} compressed rows"
+                )
+            self.decode_staging = [flat[n][: need[n]].view(S, store.pitch[n]) for n in PARAMS]
+        self.ram_view = [store.view[n] for n in PARAMS]
+        self.side = torch.cuda.Stream(device=device)
+
+    # ---- decode (experts.py:380-453) ----
+
+    def decode(self, topk_ids: torch.Tensor, gather_events: list | None = None) -> DecodeResult:
+        """Page in this step's experts; returns the cache slab and expert_map.
+
+        ``gather_events``: if a list, a (start, end) pair of timing events around
+        the first gather launch is appended (for the benchmark's roofline).
+        """
+        store, layer = self.store, self.layer
+        todo, ssd_todo = self.acquire(topk_ids)
+        dst_row, src_row = self.acquire.vram_slot, self.acquire.ram_slot
+        cached_row = self.vram.no_cache
+        base = layer * store.ram_slots
+        lut = store.layer_lut(layer)
+        staging = self.decode_staging
+        rows = (
+            self.ram_view, self.cache_rows[:2], self.cache_rows[:2],
+            [t.view(torch.int32) for t in staging] if staging is not None else None,
+            self.scale_rows, self.cache_rows[2:],
+        )  # fmt: skip
+        if gather_events is not None:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record()
+        gather_rows(todo, dst_row, cached_row, src_row, base, *rows,
+                    fetch=(ssd_todo, layer, store))
+        if gather_events is not None:
+            ev[1].record()
+            gather_events.append(ev)
+        if store.compress:
+            codec.decode_rows(todo, dst_row, cached_row, staging, self.cache_bytes, lut,
+                              skip=ssd_todo)
+        gather_rows(ssd_todo, dst_row, cached_row, src_row, base, *rows)
+        if store.compress:
+            codec.decode_rows(ssd_todo, dst_row, cached_row, staging, self.cache_bytes, lut)
+        return DecodeResult(self.cache_slab, self.expert_map)
+
+    # ---- working path (experts.py:455-577) ----
+
+    def plan(self, topk_ids: torch.Tensor):
+        """Update the RAM table and lay the step's experts out in chunks (experts.py:501-510)."""
+        store, E = self.store, self.num_experts
+        W = self.working.rows
+        need = self.ram.need_mask(topk_ids)
+        cached_row = self.vram.slot_of[:E]
+        before = self.ram.slot_of[:E].clone()
+        if topk_ids.numel() <= store.ram_slots:
+            self.ram.acquire(topk_ids)
+        else:
+            self.ram.seed(self.vram, topk_ids, need)
+        return cached_row, self.ram.plan_chunks(before, need, cached_row, W,
+                                                self.layer * store.ram_slots, store.working_base)
+
+    def working_chunks(self, topk_ids: torch.Tensor, run_chunk, overlap: bool = True):
+        """Run the working path; ``run_chunk(k, n, slabs, expert_map)`` runs chunk k's MoE.
+
+        With ``overlap`` chunk k+1's copies go to the other half of the working
+        slab on a side stream while chunk k's MoE runs on the current stream.
+        Returns the last ``run_chunk`` result.
+        """
+        store, layer = self.store, self.layer
+        W = self.working.rows
+        cached_row, (dst_row, src_row, maps, todo, ssd, late) = self.plan(topk_ids)
+        N = maps.shape[0]
+        lut = store.layer_lut(layer)
+        tickets = store.ticket_chunk
+        halves = self.working.halves if overlap else 1
+        staging = self.working.staging
+        main = torch.cuda.current_stream(store.device)
+        side = self.side if overlap else main
+
+        def rows(h):
+            wr = self.working_rows[h]
+            stg = None
+            if staging is not None:
+                stg = [t[h * W : (h + 1) * W].view(torch.int32) for t in staging]
+            return (self.ram_view, self.cache_rows[:2], wr[:2], stg, self.scale_rows, wr[2:])
+
+        def copy(part, h):
+            gather_rows(part, dst_row, cached_row, src_row, 0, *rows(h))
+            if store.compress:
+                stg = [t[h * W : (h + 1) * W] for t in staging]
+                codec.decode_rows(part, dst_row, cached_row, stg, self.working_bytes[h], lut)
+
+        def chunk(t, k):
+            return t[k * W : (k + 1) * W]
+
+        def ticket(k):
+            return tickets[k % 2 : k % 2 + 1]
+
+        copied = [torch.cuda.Event() for _ in range(N)]
+        consumed = [torch.cuda.Event() for _ in range(N)]
+        out = None
+        side.wait_stream(main)  # the plan is on the main stream
+        with torch.cuda.stream(side):
+            fetch_publish_rows(chunk(ssd, 0), src_row, 0, layer, store, ticket(0))
+        for k in range(N):
+            h = k % halves
+            with torch.cuda.stream(side):
+                if k >= halves:
+                    side.wait_event(consumed[k - halves])  # the half's previous MoE is done
+                copy(chunk(todo, k), h)
+                if k + 1 < N:
+                    fetch_publish_rows(chunk(ssd, k + 1), src_row, 0, layer, store, ticket(k + 1))
+                fetch_wait_rows(chunk(ssd, k), store, ticket(k))
+                copy(chunk(late, k), h)
+                copied[k].record(side)
+            main.wait_event(copied[k])
+            self.expert_map.copy_(maps[k])
+            out = run_chunk(k, N, self.working.half(h), self.expert_map)
+            consumed[k].record(main)
+        return out
