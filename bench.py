@@ -53,6 +53,8 @@ def parse():
     p.add_argument("--window", type=int, default=512)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--ctas", type=int, default=0, help="gather CTAs (0 = library default)")
+    p.add_argument("--workload", choices=["paging", "decode"], default="paging",
+                   help="decode: only the decode-kernel measurement (for profiling)")
     return p.parse_args()
 
 
@@ -204,6 +206,90 @@ def check_slab(store, pager) -> None:
                 raise SystemExit(f"slab row {s} does not hold expert {e} ({n})")
 
 
+def hbm_peak() -> tuple[float, str]:
+    """HBM copy bandwidth from MEASURED_PEAKS.json (driver-written), else the pool fallback."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "MEASURED_PEAKS.json hbm_gbs (measured)"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback 6.65 TB/s (no MEASURED_PEAKS.json)"
+
+
+def bench_decode(device, rows_per_launch: int, launches: int = 24, distinct: int = 64,
+                 reps: int = 3) -> dict:
+    """Decode kernel alone: compressed config-1 experts staged in HBM -> raw slab rows.
+
+    ``distinct`` experts (encoded at pitch 0.89 with the native encoder) sit in a
+    staging buffer and a destination slab of as many rows, both larger than L2;
+    each launch expands ``rows_per_launch`` of them, rotating through the set.
+    Algorithmic bytes per row = used record bytes + raw bytes written + the
+    512-byte LUT, per name.
+    """
+    from vllm_expert_pager import codec, synthetic
+
+    names = list(synthetic.SHAPES)
+    gen = torch.Generator().manual_seed(0)
+    recs = {n: [] for n in names}
+    luts = torch.zeros((distinct, 2, 512), dtype=torch.uint8)
+    used = 0
+    for e in range(distinct):
+        ex = synthetic.fp8_expert(gen) if e < 8 else None
+        for k, n in enumerate(names):
+            if ex is None:  # reuse the 8 generated experts' bytes, shifted, to save host time
+                raw = recs[n][e % 8][1]
+            else:
+                raw = synthetic.row_bytes(ex[n][0])
+            pitch = codec.pitch_of(raw.numel(), 0.89, 4096)
+            rec, lut = codec.encode(raw, pitch)
+            G = raw.numel() // codec.GROUP
+            used += 4 * (G + 1) + raw.numel() // 2 + 4 * int(rec[4 * G : 4 * G + 4].view(torch.int32))
+            recs[n].append((rec, raw))
+            luts[e, k] = lut
+    stg = [torch.stack([r for r, _ in recs[n]]).to(device) for n in names]
+    dst = [torch.empty((distinct, recs[n][0][1].numel()), dtype=torch.uint8, device=device)
+           for n in names]
+    lut_d = luts.to(device)
+    raw_bytes = sum(recs[n][0][1].numel() for n in names)
+    per_row = used / distinct + raw_bytes + 2 * 512
+    K = rows_per_launch
+    starts = list(range(0, distinct - K + 1, K))
+    todos = [torch.arange(s0, s0 + K, dtype=torch.int64, device=device) for s0 in starts]
+    ident = torch.arange(distinct, dtype=torch.int64, device=device)
+    no_cache = torch.full((distinct,), -1, dtype=torch.int64, device=device)
+
+    def launch(i):
+        # launch i expands experts [s0, s0+K): staging row j holds expert s0+j, whose
+        # raw row goes to dst row s0+j (dst_row = identity)
+        s0 = starts[i % len(starts)]
+        codec.decode_rows(todos[i % len(starts)], ident, no_cache,
+                          [x[s0 : s0 + K] for x in stg], dst, lut_d)
+
+    for i in range(4):
+        launch(i)
+    torch.cuda.synchronize()
+    best = None
+    for _ in range(reps):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(launches)]
+        for i in range(launches):
+            ev[i][0].record()
+            launch(i)
+            ev[i][1].record()
+        torch.cuda.synchronize()
+        us = sum(a.elapsed_time(b) for a, b in ev) * 1e3 / launches
+        best = us if best is None else min(best, us)
+    for n, d, k in zip(names, dst, range(2)):  # parity spot check: expanded rows == raw rows
+        for e in range(0, distinct, 17):
+            if not torch.equal(d[e].cpu(), recs[n][e][1]):
+                raise SystemExit(f"decode mismatch: expert {e} {n}")
+    peak, src = hbm_peak()
+    achieved = K * per_row / (best * 1e-6) / 1e9
+    return {"rows_per_launch": K, "us_per_launch": round(best, 2),
+            "algorithmic_bytes_per_launch": int(K * per_row), "achieved": round(achieved, 1),
+            "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "bound": "hbm",
+            "peak_source": src}
+
+
 def cpu_port(trace: np.ndarray, steps: int, src_ptrs, slab, threads: int) -> tuple[float, float]:
     """The reference's algorithm on the host: both LRU tables + memcpy of the missed rows.
 
@@ -279,6 +365,10 @@ def main():
     device = torch.device("cuda", local)
     from vllm_expert_pager import gather as gather_mod
 
+    if args.workload == "decode":
+        for k in (8, 64):
+            print(json.dumps({"decode": bench_decode(device, k)}), flush=True)
+        return
     if args.ctas:
         gather_mod.GATHER_CTAS = args.ctas
     store, pager, trace_cpu = build_workload(device)
@@ -351,6 +441,8 @@ def main():
     e2e = total_e / (e_ms_max * 1e-3) / 1e9
     achieved = moved / (gather_ms * 1e-3) / 1e9 if gather_ms > 0 else None
 
+    kernels = {"decode_k8": bench_decode(device, 8), "decode_k64": bench_decode(device, 64)}
+
     cpu = None
     if rank == 0 and world == 1:
         threads = os.cpu_count() or 1
@@ -388,6 +480,7 @@ def main():
                          "peak_source": "measured in bench.py: copy engine pinned->device, "
                                         "1 GiB, best of 6 (MEASURED_PEAKS.json has no host-link "
                                         "figure)"},
+            "kernels": kernels,
             "gpu_launches": args.steps * W * 3,
             "cpu_baseline": cpu,
             "clocks": clocks.summary(),

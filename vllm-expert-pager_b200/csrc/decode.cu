@@ -11,15 +11,21 @@
 // of at most 9 bits looked up in a 512-entry LUT (sym << 4 | len); output byte
 // = (s & 8) << 4 | sym << 3 | (s & 7) with s the stored sign/mantissa nibble.
 //
-// B200 mapping: one warp per group, several groups per CTA.
-//  * The group's Huffman words arrive in refill order, so the warp holds a
-//    96-word window in three registers per lane and hands each refilling lane
-//    its word with two shuffles; the window slides by 32 words with one
-//    coalesced load issued 32..64 words before its use.
-//  * LUT lookups go to a 128-byte first-level table in shared memory: 32 words
-//    in 32 distinct banks, so a warp's 32 random lookups never conflict.  Codes
-//    longer than 7 bits (rare) fall back to the full 512-byte table.
-//  * Nibble words are read coalesced (word m of all 32 lanes is contiguous).
+// B200 mapping: one warp per group, four groups per CTA.
+//  * The group's Huffman words are copied into shared memory first (cp.async,
+//    16 bytes per lane per step, zero-filled past the record end).  Refilling
+//    lanes then read consecutive words (ballot + popc give each its slot), so
+//    a refill is one conflict-free shared load.  A group larger than the
+//    per-warp buffer (flat exponent histograms only) takes a slower path that
+//    streams the words through a register window.
+//  * LUT lookups go to a 128-byte first-level table: its 32 words sit in 32
+//    distinct banks, so a warp's lookups never conflict.  Codes longer than 7
+//    bits (rare) fall back to the full 512-byte table.
+//  * Exponent bits of 4 symbols are summed into one word with one multiply-add
+//    each (the bit fields do not overlap) and masked once; sign/mantissa
+//    nibbles are spread to bytes with six bit operations per 4 values.
+//  * Each lane stores 16 bytes per 16 symbols; nibble words are prefetched
+//    four steps ahead.
 #include "common.cuh"
 
 namespace xp {
@@ -28,6 +34,7 @@ namespace {
 constexpr int kWarps = 4;
 constexpr int kLimit = 9;
 constexpr int kLutBytes = 512;
+constexpr int kStageWords = 2048;  // per-warp shared buffer for a group's Huffman words
 constexpr unsigned kFull = 0xffffffffu;
 
 struct DName {
@@ -48,60 +55,64 @@ struct DecodeArgs {
   int64_t chunk;
 };
 
-__global__ void __launch_bounds__(kWarps * 32) decode_kernel(const __grid_constant__ DecodeArgs a) {
-  __shared__ __align__(16) uint8_t s_lut[kWarps][kLutBytes];
-  __shared__ __align__(16) uint8_t s_lut1[kWarps][128];
-  const int64_t j = blockIdx.y;
-  const int64_t e = a.todo[j];
-  if (e < 0) return;
-  if (a.skip)
-    for (int64_t k = 0; k < a.K; ++k)
-      if (a.skip[k] == e) return;
-  if (a.cache_row[e] >= 0) return;  // copied raw from the cache slab
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t gg = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
-  if (gg >= a.n[0].G + a.n[1].G) return;
-  const int which = gg < a.n[0].G ? 0 : 1;
-  const DName &n = a.n[which];
-  const int64_t g = which ? gg - a.n[0].G : gg;
-  int64_t dst_row = a.dst_row[e];
-  dst_row = dst_row > 0 ? dst_row : 0;
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem, int src_bytes) {
+  unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem),
+               "r"(src_bytes)
+               : "memory");
+}
 
-  // This row's LUT, and its conflict-free 7-bit first level (0 = longer code).
-  uint8_t *L = s_lut[warp];
-  uint8_t *L1 = s_lut1[warp];
-  reinterpret_cast<uint4 *>(L)[lane] =
-      reinterpret_cast<const uint4 *>(a.lut + (e * 2 + which) * kLutBytes)[lane];
-  __syncwarp();
-  for (int i = lane; i < 128; i += 32) {
-    uint8_t v = L[i];
-    L1[i] = (v & 15) <= 7 ? v : 0;
-  }
-  __syncwarp();
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
 
-  const int64_t chunk = a.chunk, G = n.G;
-  const uint8_t *rec = n.stg + j * n.P;
-  const int64_t head = 4 * (G + 1);
-  const int32_t *hdr = reinterpret_cast<const int32_t *>(rec);
-  const uint32_t *nib = reinterpret_cast<const uint32_t *>(rec + head) + g * (chunk / 8) * 32;
-  const uint32_t *huff = reinterpret_cast<const uint32_t *>(rec + head + n.N / 2);
-  // Words of this group: [gstart[g], gstart[g+1]), never past the record.
-  const int64_t maxw = (n.P - head - n.N / 2) / 4;
-  const int64_t rend = hdr[g + 1] < maxw ? hdr[g + 1] : maxw;
-  int64_t wbase = hdr[g];
+// Four sign/mantissa nibbles (x: bits 0..15) -> bytes (s & 7) | (s & 8) << 4.
+__device__ __forceinline__ uint32_t spread(uint32_t x) {
+  uint32_t t = (x | (x << 8)) & 0x00FF00FFu;
+  t = (t | (t << 4)) & 0x0F0F0F0Fu;
+  return (t & 0x07070707u) | ((t << 4) & 0x80808080u);
+}
+
+// One symbol for lane state (buf, level): refill (warp-collective), look up,
+// consume.  Returns the LUT entry.  `words` is the group's staged word stream,
+// `rp` the next unread word.
+__device__ __forceinline__ uint32_t step_staged(uint64_t &buf, int &level, int &rp,
+                                                const uint32_t *words, const uint8_t *L1,
+                                                const uint8_t *L, unsigned lt) {
+  const bool need = level < kLimit;
+  const unsigned bal = __ballot_sync(kFull, need);
+  // This lane's word is the popc-th after rp; the mask keeps every read inside
+  // the warp's buffer (a refilling lane of a valid record never leaves its
+  // group's words).
+  const uint32_t w = words[(rp + __popc(bal & lt)) & (kStageWords - 1)];
+  // buf |= w << level as one wide multiply-add (the new bits are above level).
+  const uint32_t mul = need ? (1u << level) : 0u;
+  buf += static_cast<uint64_t>(w) * mul;
+  level += need ? 32 : 0;
+  rp += __popc(bal);
+  uint32_t ent = L1[static_cast<uint32_t>(buf) & 127u];
+  if ((ent & 15u) == 0) ent = L[static_cast<uint32_t>(buf) & (kLutBytes - 1)];
+  const uint32_t len = ent & 15u;
+  buf >>= len;
+  level -= static_cast<int>(len);
+  return ent;
+}
+
+// Slow path for a group whose words do not fit the shared buffer: a 96-word
+// register window slid with coalesced loads, words handed out by shuffles.
+__device__ void decode_group_window(const uint32_t *huff, int64_t wbase, int64_t rend,
+                                    const uint32_t *nib, uint8_t *out_row, int64_t chunk,
+                                    const uint8_t *L1, const uint8_t *L, int lane) {
   auto ld = [&](int64_t idx) -> uint32_t {
     return (idx >= 0 && idx < rend) ? __ldg(huff + idx) : 0u;
   };
   uint32_t w0 = ld(wbase + lane), w1 = ld(wbase + 32 + lane), w2 = ld(wbase + 64 + lane);
-  uint64_t *out = reinterpret_cast<uint64_t *>(n.dst + dst_row * n.N + (g * 32 + lane) * chunk);
-
+  uint64_t *out = reinterpret_cast<uint64_t *>(out_row);
   uint64_t buf = 0;
-  int level = 0, rel = 0;  // rel: next word of the group relative to wbase, < 32
+  int level = 0, rel = 0;
   const unsigned lt = lanemask_lt();
-  uint32_t nw_next = __ldg(nib + lane);
   for (int64_t m = 0; m < chunk / 8; ++m) {
-    const uint32_t nw = nw_next;
-    if (m + 1 < chunk / 8) nw_next = __ldg(nib + (m + 1) * 32 + lane);
+    const uint32_t nw = __ldg(nib + m * 32 + lane);
     uint32_t lo = 0, hi = 0;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
@@ -138,6 +149,113 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(const __grid_consta
   }
 }
 
+__global__ void __launch_bounds__(kWarps * 32) decode_kernel(const __grid_constant__ DecodeArgs a) {
+  __shared__ __align__(16) uint32_t s_words[kWarps][kStageWords];
+  __shared__ __align__(16) uint8_t s_lut[kWarps][kLutBytes];
+  __shared__ __align__(16) uint8_t s_lut1[kWarps][128];
+  const int64_t j = blockIdx.y;
+  const int64_t e = a.todo[j];
+  if (e < 0) return;
+  if (a.skip)
+    for (int64_t k = 0; k < a.K; ++k)
+      if (a.skip[k] == e) return;
+  if (a.cache_row[e] >= 0) return;  // copied raw from the cache slab
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t gg = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
+  if (gg >= a.n[0].G + a.n[1].G) return;
+  const int which = gg < a.n[0].G ? 0 : 1;
+  const DName &n = a.n[which];
+  const int64_t g = which ? gg - a.n[0].G : gg;
+  int64_t dst_row = a.dst_row[e];
+  dst_row = dst_row > 0 ? dst_row : 0;
+  const int64_t chunk = a.chunk, G = n.G;
+  const uint8_t *rec = n.stg + j * n.P;
+  const int64_t head = 4 * (G + 1);
+  const int32_t *hdr = reinterpret_cast<const int32_t *>(rec);
+  const int64_t huff_w = (head + n.N / 2) / 4;  // first Huffman word, from the record start
+  const int64_t rec_w = n.P / 4;
+  // Words of this group: [gstart[g], gstart[g+1]), never past the record.
+  int64_t w_begin = hdr[g], w_end = hdr[g + 1];
+  if (w_end > rec_w - huff_w) w_end = rec_w - huff_w;
+  if (w_begin > w_end) w_begin = w_end;
+
+  uint8_t *L = s_lut[warp];
+  uint8_t *L1 = s_lut1[warp];
+  reinterpret_cast<uint4 *>(L)[lane] =
+      reinterpret_cast<const uint4 *>(a.lut + (e * 2 + which) * kLutBytes)[lane];
+  __syncwarp();
+  for (int i = lane; i < 128; i += 32) {
+    uint8_t v = L[i];
+    L1[i] = (v & 15) <= 7 ? v : 0;
+  }
+  const uint32_t *nib = reinterpret_cast<const uint32_t *>(rec + head) + g * (chunk / 8) * 32;
+  uint8_t *out_row = n.dst + dst_row * n.N + (g * 32 + lane) * chunk;
+
+  // Copy the group's words into shared memory in 16-byte units aligned to the
+  // record (4096-aligned rows, so record word 4u is 16-byte aligned).
+  const int64_t a_begin = huff_w + w_begin, a_end = huff_w + w_end;
+  const int64_t a0 = a_begin & ~int64_t(3);
+  const int64_t units = (a_end - a0 + 3) / 4;
+  const bool staged = units * 4 <= kStageWords && (chunk / 8) % 2 == 0;
+  if (!staged) {
+    __syncwarp();
+    decode_group_window(reinterpret_cast<const uint32_t *>(rec) + huff_w, w_begin,
+                        w_end, nib, out_row, chunk, L1, L, lane);
+    return;
+  }
+  uint32_t *words = s_words[warp];
+  for (int64_t u = lane; u < units; u += 32) {
+    const int64_t w = a0 + 4 * u;
+    int64_t bytes = (rec_w - w) * 4;
+    bytes = bytes < 0 ? 0 : (bytes > 16 ? 16 : bytes);
+    cp_async16(words + 4 * u, rec + 4 * (bytes > 0 ? w : 0), static_cast<int>(bytes));
+  }
+  cp_async_wait_all();
+  __syncwarp();
+
+  const unsigned lt = lanemask_lt();
+  uint64_t buf = 0;
+  int level = 0;
+  int rp = static_cast<int>(a_begin - a0);
+  const int64_t steps = chunk / 8;
+  uint32_t q0 = __ldg(nib + lane);
+  uint32_t q1 = steps > 1 ? __ldg(nib + 32 + lane) : 0u;
+  uint32_t q2 = steps > 2 ? __ldg(nib + 64 + lane) : 0u;
+  uint32_t q3 = steps > 3 ? __ldg(nib + 96 + lane) : 0u;
+  uint4 *out = reinterpret_cast<uint4 *>(out_row);
+  for (int64_t m = 0; m < steps; m += 2) {
+    uint32_t lohi[4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t nw = h ? q1 : q0;
+      uint32_t acc_lo, acc_hi;
+      {
+        uint32_t ent = step_staged(buf, level, rp, words, L1, L, lt);
+        acc_lo = ent >> 1;
+#pragma unroll
+        for (int k = 1; k < 4; ++k) {
+          ent = step_staged(buf, level, rp, words, L1, L, lt);
+          acc_lo += ent << (8 * k - 1);
+        }
+        ent = step_staged(buf, level, rp, words, L1, L, lt);
+        acc_hi = ent >> 1;
+#pragma unroll
+        for (int k = 1; k < 4; ++k) {
+          ent = step_staged(buf, level, rp, words, L1, L, lt);
+          acc_hi += ent << (8 * k - 1);
+        }
+      }
+      lohi[2 * h] = (acc_lo & 0x78787878u) | spread(nw & 0xFFFFu);
+      lohi[2 * h + 1] = (acc_hi & 0x78787878u) | spread(nw >> 16);
+    }
+    out[m / 2] = make_uint4(lohi[0], lohi[1], lohi[2], lohi[3]);
+    q0 = q2;
+    q1 = q3;
+    q2 = m + 4 < steps ? __ldg(nib + (m + 4) * 32 + lane) : 0u;
+    q3 = m + 5 < steps ? __ldg(nib + (m + 5) * 32 + lane) : 0u;
+  }
+}
+
 }  // namespace
 }  // namespace xp
 
@@ -164,9 +282,12 @@ extern "C" int xp_decode_rows(const int64_t *todo, int64_t K, const int64_t *dst
   const int64_t Ps[2] = {P0, P1}, Ns[2] = {N0, N1};
   for (int i = 0; i < 2; ++i) {
     const int64_t N = Ns[i], P = Ps[i];
-    if (N <= 0 || N % (32 * chunk) || P % 4 || P < 4 * (N / (32 * chunk) + 1) + N / 2)
+    if (N <= 0 || N % (32 * chunk) || P % 16 || P < 4 * (N / (32 * chunk) + 1) + N / 2)
       return XP_EINVAL;
-    if (!stgs[i] || !dsts[i] || !aligned(stgs[i], 4) || !aligned(dsts[i], 8)) return XP_EINVAL;
+    // Records start on 16-byte boundaries (cp.async); the 16-byte output stores
+    // need 16-byte aligned lane chunks.
+    if (!stgs[i] || !dsts[i] || !aligned(stgs[i], 16) || !aligned(dsts[i], 16))
+      return XP_EINVAL;
     a.n[i] = DName{static_cast<const uint8_t *>(stgs[i]), P, static_cast<uint8_t *>(dsts[i]), N,
                    N / (32 * chunk)};
   }
