@@ -56,6 +56,30 @@ def fp8_experts(count: int, seed: int = 0):
     return [fp8_expert(gen) for _ in range(count)]
 
 
+def fp8_experts_device(count: int, device: torch.device, seed: int = 0, batch: int = 32):
+    """``count`` experts drawn on the device (torch's CUDA generator seeded ``seed``).
+
+    Same distribution and quantisation as ``fp8_expert`` but generated
+    ``batch`` experts at a time on the GPU (the CPU generator is too slow for
+    hundreds of experts).  Returns ``{name: (fp8 [count, r, c], fp32 scales
+    [count, r/128, c/128])}``.
+    """
+    gen = torch.Generator(device=device).manual_seed(seed)
+    out = {}
+    for name, (r, c) in SHAPES.items():
+        q = torch.empty((count, r, c), dtype=torch.float8_e4m3fn, device=device)
+        sc = torch.empty((count, r // BLOCK, c // BLOCK), dtype=torch.float32, device=device)
+        for e0 in range(0, count, batch):
+            n = min(batch, count - e0)
+            w = (torch.randn((n, r, c), generator=gen, device=device) * 0.02).to(torch.bfloat16)
+            blocks = w.float().view(n, r // BLOCK, BLOCK, c // BLOCK, BLOCK)
+            amax = blocks.abs().amax(dim=(2, 4)) / FP8_MAX
+            q[e0 : e0 + n] = (blocks / amax[:, :, None, :, None]).to(torch.float8_e4m3fn).view(n, r, c)
+            sc[e0 : e0 + n] = amax
+        out[name] = (q, sc)
+    return out
+
+
 def row_bytes(q: torch.Tensor) -> torch.Tensor:
     """The raw bytes of a weight as a flat uint8 tensor."""
     return q.contiguous().view(torch.uint8).reshape(-1)
