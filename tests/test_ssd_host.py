@@ -1,0 +1,229 @@
+"""The host SSD server and its request-ring protocol, without a GPU.
+
+A Python thread plays the GPU side of the ring (the reference's
+``_fetch_publish``/``_fetch_wait``, gather.py:197-277): it fills a request slot,
+stores ``seq`` last, and waits for ``done``.  The server under test is this
+repository's C++ server (``libxpager.so``); when ``oracle/_ref/libssd_ref.so``
+was built from the reference's own C server (oracle/build_ref.py), every
+scenario also runs against it and the outcomes must agree: RAM-tier rows,
+``done``, statistics and error text.  (x86 keeps the order of the two plain
+stores, so the Python publisher needs no fence.)
+"""
+
+import ctypes
+import os
+import time
+
+import numpy as np
+import pytest
+
+from vllm_expert_pager import native
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REF = os.path.join(os.path.dirname(HERE), "oracle", "_ref", "libssd_ref.so")
+RING = 4
+PITCH = (8192, 4096)
+
+
+def load_server(path):
+    if path is None:
+        return native.lib()
+    so = ctypes.CDLL(path)
+    so.ssd_start.restype = ctypes.c_void_p
+    so.ssd_start.argtypes = ([ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p] + [ctypes.c_long] * 6
+                             + [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int])
+    so.ssd_stop.argtypes = [ctypes.c_void_p]
+    so.ssd_stats.argtypes = [ctypes.c_void_p] + [ctypes.POINTER(ctypes.c_long)] * 2 + [
+        ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_long)]
+    so.ssd_error.restype = ctypes.c_char_p
+    so.ssd_error.argtypes = [ctypes.c_void_p]
+    so.ssd_test_delay.argtypes = [ctypes.c_void_p, ctypes.c_double]
+    return so
+
+
+SERVERS = [None] + ([REF] if os.path.exists(REF) else [])
+IDS = ["xpager"] + (["reference"] if os.path.exists(REF) else [])
+
+
+def aligned(nbytes: int) -> np.ndarray:
+    raw = np.zeros(nbytes + 4096, dtype=np.uint8)
+    off = (-raw.ctypes.data) % 4096
+    return raw[off : off + nbytes]
+
+
+class Ring:
+    """The pinned ring, RAM-tier rows and paging file of one server instance."""
+
+    def __init__(self, so, tmp_path, L, E, R, working=2, workers=7):
+        self.so, self.L, self.E, self.R = so, L, E, R
+        self.block = 1 << (E - 1).bit_length()
+        self.slot_words = 2 + 2 * self.block
+        self.req = np.zeros(2 + RING * self.slot_words, dtype=np.int64)
+        self.done = np.zeros(1, dtype=np.int64)
+        self.rows = L * R + working
+        self.record = sum(PITCH)
+        self.pinned = [aligned(self.rows * p) for p in PITCH]
+        rng = np.random.default_rng(L * 1000 + E)
+        self.file = rng.integers(0, 256, L * E * self.record, dtype=np.uint8)
+        path = str(tmp_path / f"pager-{id(self)}.bin")
+        self.file.tofile(path)
+        try:
+            self.fd = os.open(path, os.O_RDONLY | os.O_DIRECT)
+        except OSError:
+            self.fd = os.open(path, os.O_RDONLY)
+        ptrs = (ctypes.c_void_p * 2)(*(p.ctypes.data for p in self.pinned))
+        pitch = (ctypes.c_long * 2)(*PITCH)
+        self.h = so.ssd_start(self.fd, ctypes.c_void_p(self.req.ctypes.data),
+                              ctypes.c_void_p(self.done.ctypes.data), RING, self.block, L, E,
+                              self.rows, self.record, 2, ptrs, pitch, workers)
+        assert self.h
+        self.seq = 0
+
+    def publish(self, layer, experts, rows, seq=None):
+        self.seq = self.seq + 1 if seq is None else seq
+        s = 2 + (self.seq % RING) * self.slot_words
+        self.req[s + 2 : s + 2 + 2 * self.block] = -1
+        self.req[s + 2 : s + 2 + len(experts)] = experts
+        self.req[s + 2 + self.block : s + 2 + self.block + len(rows)] = rows
+        self.req[s + 1] = layer
+        self.req[s] = self.seq  # last
+        return self.seq
+
+    def wait(self, seq, timeout=10.0):
+        t0 = time.time()
+        while self.done[0] < seq:
+            if time.time() - t0 > timeout:
+                raise TimeoutError(f"done={self.done[0]} < {seq}")
+            time.sleep(0.0005)
+
+    def stats(self):
+        f, r, m = ctypes.c_long(), ctypes.c_long(), ctypes.c_long()
+        io = ctypes.c_double()
+        self.so.ssd_stats(ctypes.c_void_p(self.h), ctypes.byref(f), ctypes.byref(r),
+                          ctypes.byref(io), ctypes.byref(m))
+        return f.value, r.value, m.value
+
+    def error(self):
+        e = self.so.ssd_error(ctypes.c_void_p(self.h))
+        return None if e is None else e.decode()
+
+    def row(self, k, row):
+        p = PITCH[k]
+        return self.pinned[k][row * p : (row + 1) * p]
+
+    def expected(self, k, layer, e):
+        off = (layer * self.E + e) * self.record + sum(PITCH[:k])
+        return self.file[off : off + PITCH[k]]
+
+    def close(self):
+        self.so.ssd_stop(ctypes.c_void_p(self.h))
+        os.close(self.fd)
+
+
+@pytest.fixture(params=SERVERS, ids=IDS)
+def server(request, tmp_path):
+    so = load_server(request.param)
+    made = []
+
+    def make(*a, **k):
+        r = Ring(so, tmp_path, *a, **k)
+        made.append(r)
+        return r
+
+    yield make
+    for r in made:
+        r.close()
+
+
+def test_serves_requests_in_order(server):
+    r = server(2, 8, 4)
+    for i in range(20):
+        a, b = 4 + i % 4, 4 + (i + 1) % 4
+        rows = [1 * 4 + i % 4, 1 * 4 + (i + 1) % 4]
+        r.wait(r.publish(1, [a, b], rows))
+        for k in range(2):
+            assert np.array_equal(r.row(k, rows[0]), r.expected(k, 1, a))
+            assert np.array_equal(r.row(k, rows[1]), r.expected(k, 1, b))
+    assert r.stats() == (20, 40, 0) and r.error() is None
+
+
+def test_many_experts_in_one_request(server):
+    r = server(1, 32, 16, workers=7)
+    r.wait(r.publish(0, list(range(16, 32)), list(range(16))))
+    for s in range(16):
+        for k in range(2):
+            assert np.array_equal(r.row(k, s), r.expected(k, 0, 16 + s))
+    assert r.stats() == (1, 16, 0)
+
+
+def test_failed_read_still_writes_done(server):
+    r = server(2, 8, 4)
+    r.wait(r.publish(1, [4, 5], [10**6, 0]))
+    assert r.error() is not None and "outside the RAM tier" in r.error()
+    assert np.array_equal(r.row(0, 0), r.expected(0, 1, 5))
+
+
+def test_out_of_range_expert_is_an_error(server):
+    r = server(2, 8, 4)
+    r.wait(r.publish(1, [9], [0]))
+    assert "out of range" in r.error()
+
+
+def test_gap_in_seq_counts_missed(server):
+    # The server watches slot (last+1) % RING.  Requests 2..5 never reached it
+    # (given up by the "GPU"); request 6 lands in the same slot as 2.
+    r = server(2, 8, 4)
+    r.wait(r.publish(0, [5], [0]))
+    r.wait(r.publish(0, [6], [1], seq=2 + RING))
+    assert r.stats()[2] == RING
+    assert np.array_equal(r.row(0, 1), r.expected(0, 0, 6))
+
+
+def test_rewrites_done_when_republish_counter_moves(server):
+    r = server(2, 8, 4)
+    seq = r.publish(1, [4], [4])
+    r.wait(seq)
+    r.done[0] = 0
+    r.req[0] += 1
+    r.wait(seq, timeout=5)
+
+
+def test_test_delay_holds_the_request(server):
+    r = server(2, 8, 4)
+    r.so.ssd_test_delay(ctypes.c_void_p(r.h), 0.3)
+    t0 = time.time()
+    r.wait(r.publish(1, [4], [4]))
+    assert time.time() - t0 >= 0.25
+    r.so.ssd_test_delay(ctypes.c_void_p(r.h), 0.0)
+
+
+def test_ring_wraps_with_outstanding_requests(server):
+    """Up to RING requests may be outstanding; done advances in order."""
+    r = server(2, 16, 8)
+    seqs = [r.publish(i % 2, [8 + i], [(i % 2) * 8 + i]) for i in range(RING - 1)]
+    r.wait(seqs[-1])
+    for i in range(RING - 1):
+        for k in range(2):
+            assert np.array_equal(r.row(k, (i % 2) * 8 + i), r.expected(k, i % 2, 8 + i))
+
+
+@pytest.mark.skipif(not os.path.exists(REF), reason="reference server not built")
+def test_random_sequence_matches_reference_server(tmp_path):
+    """The same 60 random requests through both servers leave identical RAM tiers and stats."""
+    rng = np.random.default_rng(5)
+    rings = [Ring(load_server(p), tmp_path, 3, 24, 8) for p in (None, REF)]
+    try:
+        for _ in range(60):
+            layer = int(rng.integers(0, 3))
+            n = int(rng.integers(1, 9))
+            experts = rng.choice(24, n, replace=False).tolist()
+            rows = rng.choice(3 * 8 + 2, n, replace=False).tolist()
+            for ring in rings:
+                ring.wait(ring.publish(layer, experts, rows))
+        a, b = rings
+        for k in range(2):
+            assert np.array_equal(a.pinned[k], b.pinned[k])
+        assert a.stats() == b.stats() and a.error() == b.error() is None
+    finally:
+        for ring in rings:
+            ring.close()
