@@ -53,8 +53,12 @@ def parse():
     p.add_argument("--window", type=int, default=512)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--ctas", type=int, default=0, help="gather CTAs (0 = library default)")
-    p.add_argument("--workload", choices=["paging", "decode"], default="paging",
-                   help="decode: only the decode-kernel measurement (for profiling)")
+    p.add_argument("--workload", choices=["paging", "decode", "model", "compressed", "prefill"],
+                   default="paging",
+                   help="paging: config 2 (the headline line); decode: the decode kernel alone; "
+                        "model/compressed/prefill: configs 3/4/5 on a paged 40-layer MoE")
+    p.add_argument("--layers", type=int, default=40, help="MoE layers of configs 3-5")
+    p.add_argument("--tokens", type=int, default=512, help="decode tokens of configs 3-4")
     return p.parse_args()
 
 
@@ -290,6 +294,292 @@ def bench_decode(device, rows_per_launch: int, launches: int = 24, distinct: int
             "peak_source": src}
 
 
+class PagedMoE:
+    """A Qwen3-style MoE stack (hidden 2048, moe_inter 512, 256 experts, top-8, FP8
+    128x128 block scales, random-init weights and routers) whose expert weights
+    are paged: one LayerPager per layer, one Store, one shared working slab.
+
+    The 256 x layers experts are drawn from a pool of ``pool`` distinct seeded
+    experts (layer l, expert e -> pool[perm_l[e]]), so that loading the RAM
+    tier and writing the paging file of 40 layers takes seconds; every (layer,
+    expert) row is still a separate record read over the host link or from
+    the SSD.
+    """
+
+    def __init__(self, device, layers=40, S=32, R=256, compress=False, path=None, W=64,
+                 overlap=True, pool=64, seed=0):
+        from concurrent.futures import ThreadPoolExecutor
+
+        from vllm_expert_pager import codec, moe, synthetic
+        from vllm_expert_pager.pager import PARAMS, LayerPager, WorkingSlab
+        from vllm_expert_pager.store import Store
+
+        self.device, self.L, self.S, self.overlap = device, layers, S, overlap
+        row_bytes = {n: r * c for n, (r, c) in synthetic.SHAPES.items()}
+        self.store = store = Store(layers, E, R, 2 * W, row_bytes, compress, 0.89, path, device)
+        pw = synthetic.fp8_experts_device(pool, device, seed=seed)
+        g = torch.Generator().manual_seed(seed + 1)
+        self.assign = [torch.randperm(E, generator=g) % pool for _ in range(layers)]
+        recs, luts = {}, torch.zeros((pool, 2, 512), dtype=torch.uint8, device=device)
+        if compress:
+            host = {n: pw[n][0].cpu() for n in PARAMS}
+            jobs = [(p, k, n) for p in range(pool) for k, n in enumerate(PARAMS)]
+
+            def enc(job):
+                p, k, n = job
+                raw = host[n][p].view(torch.uint8).reshape(-1)
+                return job, codec.encode(raw, store.pitch[n])
+
+            with ThreadPoolExecutor(os.cpu_count() or 4) as ex:
+                for (p, k, n), (rec, lut) in ex.map(enc, jobs):
+                    recs[p, n] = rec.view(torch.int32)
+                    luts[p, k] = lut.to(device)
+        for layer in range(layers):
+            a = self.assign[layer]
+            for k, n in enumerate(PARAMS):
+                if compress:
+                    rows = torch.stack([recs[int(p), n] for p in a[:R]])
+                    store.lut[layer, :, k] = luts[a.to(device), k]
+                else:
+                    rows = pw[n][0][a[:R].to(device)].view(torch.int32).reshape(R, -1).cpu()
+                store.pinned[n][layer * R : (layer + 1) * R].copy_(rows)
+            if store.fd_w is not None:  # the paging file: all E records of the layer
+                blob = torch.empty((E, store.record_bytes), dtype=torch.uint8)
+                for k, n in enumerate(PARAMS):
+                    off = store.offset[n]
+                    for e in range(E):
+                        src = recs[int(a[e]), n] if compress else \
+                            pw[n][0][int(a[e])].view(torch.int32).reshape(-1).cpu()
+                        blob[e, off : off + store.pitch[n]] = src.view(torch.uint8)
+                os.pwrite(store.fd_w, memoryview(blob.numpy()), layer * E * store.record_bytes)
+        if store.fd_w is not None:
+            os.fsync(store.fd_w)
+        self.pool_weights = pw
+        shapes = {n: (synthetic.SHAPES[n], torch.float8_e4m3fn) for n in PARAMS}
+        all_shapes = dict(shapes)
+        all_shapes.update({f"{n[:-7]}_weight_scale": (tuple(pw[n][1].shape[1:]), torch.float32)
+                           for n in PARAMS})
+        self.working = WorkingSlab(W, all_shapes, store, device, halves=2 if overlap else 1)
+        self.pagers = []
+        for layer in range(layers):
+            a = self.assign[layer].to(device)
+            scales = {f"{n[:-7]}_weight_scale": pw[n][1][a].contiguous() for n in PARAMS}
+            self.pagers.append(LayerPager(store, layer, S, scales, shapes, self.working))
+        gr = torch.Generator(device=device).manual_seed(seed + 2)
+        self.router = [(torch.randn((2048, E), generator=gr, device=device) * 0.02).to(torch.bfloat16)
+                       for _ in range(layers)]
+        self.moe = moe
+        self.configs = {}
+
+    def config(self, T):
+        if T not in self.configs:
+            self.configs[T] = self.moe.moe_config((E, 1024, 2048), (E, 2048, 512), TOPK, T)
+        return self.configs[T]
+
+    def layer(self, l, h, events=None):
+        """One MoE layer with paged experts: route, page, run vLLM's fused MoE, add residual."""
+        moe, pager = self.moe, self.pagers[l]
+        T = h.shape[0]
+        logits = (h @ self.router[l]).float()
+        w, ids = torch.softmax(logits, -1).topk(TOPK)
+        w = (w / w.sum(-1, keepdim=True)).float()
+        ids = ids.to(torch.int32)
+        cfg = self.config(T)
+        out = torch.empty_like(h)
+        if ids.numel() <= self.S:
+            res = pager.decode(ids)
+            s = res.slabs
+            c3 = moe.contributions(h, s["w13_weight"], s["w2_weight"], s["w13_weight_scale"],
+                                   s["w2_weight_scale"], w, ids, res.expert_map, E, cfg)
+            moe.moe_sum(c3, out)
+        else:
+            acc = {}
+
+            def run_chunk(k, n, s, expert_map):
+                c3 = moe.contributions(h, s["w13_weight"], s["w2_weight"],
+                                       s["w13_weight_scale"], s["w2_weight_scale"], w, ids,
+                                       expert_map, E, cfg)
+                acc["c"] = c3 if "c" not in acc else acc["c"].add_(c3)
+                if k == n - 1:
+                    moe.moe_sum(acc["c"], out)
+
+            pager.working_chunks(ids, run_chunk, overlap=self.overlap)
+        return h + out
+
+    def forward(self, h):
+        for l in range(self.L):
+            h = self.layer(l, h)
+        return h
+
+    def misses(self) -> int:
+        return sum(int(p.vram.counters[2]) for p in self.pagers)
+
+    def check(self, layers=4):
+        """Slots of the first layers hold the rows of the experts their tables name."""
+        from vllm_expert_pager.pager import PARAMS
+
+        for l in range(min(layers, self.L)):
+            p = self.pagers[l]
+            ein = p.vram.expert_in[: self.S].cpu().tolist()
+            for s, e in enumerate(ein[:4]):
+                if e < 0:
+                    continue
+                src = int(self.assign[l][e])
+                for n in PARAMS:
+                    if not torch.equal(p.cache_slab[n][s].view(torch.uint8),
+                                       self.pool_weights[n][0][src].view(torch.uint8)):
+                        raise SystemExit(f"layer {l} slot {s}: wrong rows for expert {e} ({n})")
+
+    def release(self):
+        self.store.release()
+
+
+def timed(fn, reps=1):
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        fn()
+    b.record()
+    b.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def run_model_decode(args, device, compress: bool, R: int, batch: int, tokens: int,
+                     path=None) -> dict:
+    """Configs 3 and 4: decode ``tokens`` tokens of a 40-layer paged MoE, graph-replayed."""
+    m = PagedMoE(device, layers=args.layers, S=S, R=R, compress=compress, path=path)
+    m.store.retry_ns = 500_000_000
+    gen = torch.Generator(device=device).manual_seed(11)
+    emb = (torch.randn((tokens + 16, batch, 2048), generator=gen, device=device) * 0.5).to(torch.bfloat16)
+    x = torch.empty((batch, 2048), dtype=torch.bfloat16, device=device)
+    x.copy_(emb[0])
+    for t in range(3):  # eager warm-up (Triton JIT, tables)
+        x.copy_(emb[t])
+        m.forward(x)
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream(device=device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(s):
+        m.forward(x)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            y = m.forward(x)
+    torch.cuda.synchronize()
+    for t in range(3, 8):
+        x.copy_(emb[t])
+        graph.replay()
+    torch.cuda.synchronize()
+    miss0 = m.misses()
+    reads0 = m.store.reads
+
+    def run():
+        for t in range(tokens):
+            x.copy_(emb[8 + t % 8])
+            graph.replay()
+
+    with Clocks(torch.cuda.current_device()) as clocks:
+        ms = timed(run)
+    misses = m.misses() - miss0
+    m.check()
+    res = {"layers": args.layers, "batch": batch, "tokens": tokens, "ms": round(ms, 2),
+           "tok_per_s": round(tokens * batch / (ms * 1e-3), 2),
+           "tpot_ms": round(ms / tokens, 3),
+           "paged_gb_per_s": round(misses * (m.store.record_bytes if compress else EXPERT_BYTES)
+                                   / (ms * 1e-3) / 1e9, 3),
+           "vram_misses_per_layer_step": round(misses / (tokens * args.layers), 3),
+           "ssd_reads": m.store.reads - reads0,
+           "ssd_gb_per_s": round((m.store.reads - reads0) * m.store.record_bytes
+                                 / (ms * 1e-3) / 1e9, 3),
+           "ssd_failed": m.store.failed,
+           "giveups": int(m.store.req[m.store.giveup_at]), "clocks": clocks.summary(),
+           "finite": bool(torch.isfinite(y).all())}
+    del graph
+    m.release()
+    return res
+
+
+def run_prefill(args, device, path) -> dict:
+    """Config 5: a 2048-token prefill with uniform top-8 routing through every layer,
+    compressed RAM tier (R=128) + SSD; copies overlapped with the MoE, and serial."""
+    out = {}
+    for overlap in (True, False):
+        m = PagedMoE(device, layers=args.layers, S=S, R=128, compress=True, path=path,
+                     overlap=overlap)
+        gen = torch.Generator(device=device).manual_seed(13)
+        T = 2048
+        h = (torch.randn((T, 2048), generator=gen, device=device) * 0.5).to(torch.bfloat16)
+        from vllm_expert_pager import synthetic
+
+        ids = synthetic.uniform_routing(T, seed=5).to(device)
+        w = torch.softmax(torch.randn((T, TOPK), generator=gen, device=device), -1)
+        cfg = m.config(T)
+        moe = m.moe
+
+        def layer_paged(l):
+            acc = {}
+            o = torch.empty_like(h)
+
+            def run_chunk(k, n, s, expert_map):
+                c3 = moe.contributions(h, s["w13_weight"], s["w2_weight"], s["w13_weight_scale"],
+                                       s["w2_weight_scale"], w, ids, expert_map, E, cfg)
+                acc["c"] = c3 if "c" not in acc else acc["c"].add_(c3)
+                if k == n - 1:
+                    moe.moe_sum(acc["c"], o)
+
+            m.pagers[l].working_chunks(ids, run_chunk, overlap=overlap)
+            return o
+
+        layer_paged(0)  # warm-up (JIT)
+        torch.cuda.synchronize()
+        reads0 = m.store.reads
+        ms = timed(lambda: [layer_paged(l) for l in range(args.layers)])
+        reads = m.store.reads - reads0
+        # MoE alone on resident weights (the pool), for the overlap fraction.
+        pw = m.pool_weights
+        pool_ids = (ids % pw["w13_weight"][0].shape[0]).to(torch.int32)
+        moe_ms = timed(lambda: [moe.moe_sum(moe.contributions(
+            h, pw["w13_weight"][0], pw["w2_weight"][0], pw["w13_weight"][1], pw["w2_weight"][1],
+            w, pool_ids, None, pw["w13_weight"][0].shape[0], cfg), torch.empty_like(h))
+            for _ in range(args.layers)])
+        out["overlap" if overlap else "serial"] = {
+            "ms_per_layer": round(ms / args.layers, 3), "ssd_reads": reads,
+            "ssd_gb_per_s": round(reads * m.store.record_bytes / (ms * 1e-3) / 1e9, 3),
+            "moe_only_ms_per_layer": round(moe_ms / args.layers, 3)}
+        m.release()
+    o, s_ = out["overlap"]["ms_per_layer"], out["serial"]["ms_per_layer"]
+    moe_ms = out["serial"]["moe_only_ms_per_layer"]
+    copy = max(s_ - moe_ms, 1e-9)
+    out["hidden_fraction"] = round(max(0.0, min(1.0, (s_ - o) / copy)), 3)
+    return out
+
+
+def run_model_workload(args):
+    """--workload model|compressed|prefill: configs 3, 4 and 5 (one JSON line each)."""
+    world, rank, local = dist_setup()
+    device = torch.device("cuda", local)
+    base = os.environ.get("XP_BENCH_DIR", "/tmp")
+    path = os.path.join(base, f"xpager_bench_{rank}.bin")
+    try:
+        if args.workload == "model":
+            res = {"config3": run_model_decode(args, device, False, 256, 1, args.tokens)}
+        elif args.workload == "compressed":
+            res = {"config4_batch1": run_model_decode(args, device, True, 128, 1, args.tokens,
+                                                      path),
+                   "config4_batch8": run_model_decode(args, device, True, 128, 8,
+                                                      max(args.tokens // 4, 8), path)}
+        else:
+            res = {"config5": run_prefill(args, device, path)}
+    finally:
+        if os.path.exists(path):
+            os.unlink(path)
+    res["rank"] = rank
+    print(json.dumps(res), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
 def cpu_port(trace: np.ndarray, steps: int, src_ptrs, slab, threads: int) -> tuple[float, float]:
     """The reference's algorithm on the host: both LRU tables + memcpy of the missed rows.
 
@@ -358,6 +648,9 @@ def run_reference(args, world, rank):
 
 def main():
     args = parse()
+    if args.workload in ("model", "compressed", "prefill"):
+        run_model_workload(args)
+        return
     world, rank, local = dist_setup()
     if args.impl == "reference":
         run_reference(args, world, rank)
