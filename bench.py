@@ -86,24 +86,35 @@ def barrier(world):
         dist.barrier()
 
 
-def max_over_ranks(x: float, world: int) -> float:
+def _reduce(x: float, world: int, op: str) -> float:
+    """max/sum of a per-rank scalar over all ranks (NCCL: a CUDA tensor; gloo: CPU)."""
     if world == 1:
         return x
     import torch.distributed as dist
 
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
     return float(t.item())
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    return _reduce(x, world, "max")
 
 
 def sum_over_ranks(x: float, world: int) -> float:
-    if world == 1:
-        return x
-    import torch.distributed as dist
+    return _reduce(x, world, "sum")
 
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.SUM)
-    return float(t.item())
+
+def aggregate(moved: float, ms: float, world: int) -> tuple[float, float, float]:
+    """Whole-job throughput of independent replicas: (GB/s, bytes of all ranks, slowest ms).
+
+    Every rank pages its own experts; the job moves the sum of the ranks' bytes
+    in the time of the slowest rank.
+    """
+    ms_max = max_over_ranks(ms, world)
+    total = sum_over_ranks(moved, world)
+    return total / (ms_max * 1e-3) / 1e9, total, ms_max
 
 
 class Clocks:
@@ -726,12 +737,8 @@ def main():
     e_ms = e_start.elapsed_time(e_end)
     e_moved = (int(pager.vram.counters[2]) - miss1) * EXPERT_BYTES
 
-    ms_max = max_over_ranks(ms, world)
-    e_ms_max = max_over_ranks(e_ms, world)
-    total_moved = sum_over_ranks(moved, world)
-    total_e = sum_over_ranks(e_moved, world)
-    value = total_moved / (ms_max * 1e-3) / 1e9
-    e2e = total_e / (e_ms_max * 1e-3) / 1e9
+    value, _, ms_max = aggregate(moved, ms, world)
+    e2e, _, _ = aggregate(e_moved, e_ms, world)
     achieved = moved / (gather_ms * 1e-3) / 1e9 if gather_ms > 0 else None
 
     kernels = {"decode_k8": bench_decode(device, 8), "decode_k64": bench_decode(device, 64)}
