@@ -776,12 +776,13 @@ def main():
             "roofline": {"bound": "host_link", "achieved": round(achieved, 3) if achieved else None,
                          "peak": round(peak, 3), "unit": "GB/s",
                          "frac": round(achieved / peak, 4) if achieved else None, "traffic": None,
-                         "kernel": "gather_kernel",
+                         "kernel": "step_kernel (both table updates + the gather, one launch "
+                                   "per decode step)",
                          "peak_source": "measured in bench.py: copy engine pinned->device, "
                                         "1 GiB, best of 6 (MEASURED_PEAKS.json has no host-link "
                                         "figure)"},
             "kernels": kernels,
-            "gpu_launches": args.steps * W * 3,
+            "gpu_launches": args.steps * W,
             "cpu_baseline": cpu,
             "clocks": clocks.summary(),
         }

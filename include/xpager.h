@@ -145,6 +145,38 @@ int xp_fetch(const int64_t *todo, int64_t K, const int64_t *row_of, int64_t base
              int64_t *seq, int64_t *req, const int64_t *done, int64_t block, int64_t ring,
              int64_t retry_ns, int64_t giveup, void *stream);
 
+/* Bytes of the scratch block xp_decode_step needs (zeroed once by the caller;
+ * every launch leaves it zeroed again except the error counter, word 3). */
+#define XP_STEP_SCRATCH_BYTES 16
+
+/* Replaces the decode path's three launches (experts.py:406-447: AcquirePair,
+ * gather_rows with fetch, gather_rows of the SSD misses) with one: CTA 0/1
+ * update the VRAM table a and the RAM table b exactly as xp_acquire_pair
+ * (same outputs), the copy CTAs then copy the VRAM misses from the RAM tier
+ * (src_n rows b_slot[e] + base; to dst_n[a_slot[e]] raw, or to the staging row
+ * of e's position in a_todo when compressed) with their scale rows, and, if
+ * req is not NULL, a last CTA publishes the RAM misses (b_todo) to the host
+ * server and waits as xp_fetch does, after which the copy CTAs copy those rows
+ * too.  A compressed step then needs one xp_decode_rows(a_todo, a_slot,
+ * no_cache, ...) without skip.  no_cache: int64[E] of -1.  scratch:
+ * XP_STEP_SCRATCH_BYTES of device memory, 16-byte aligned, zeroed before the
+ * first call and not shared by launches that may overlap; scratch word 3
+ * (uint32) counts waits that gave up. */
+int xp_decode_step(const void *topk_ids, int ids_bytes, int64_t K, int64_t E,
+                   int64_t *a_slot_of, int64_t *a_expert_in, int64_t *a_last_used,
+                   int64_t *a_counters, int64_t a_slots, int32_t *expert_map, int64_t *a_slot,
+                   int64_t *a_todo,
+                   int64_t *b_slot_of, int64_t *b_expert_in, int64_t *b_last_used,
+                   int64_t *b_counters, int64_t b_slots, int64_t *b_slot, int64_t *b_todo,
+                   const int64_t *no_cache, int64_t base,
+                   const void *src0, void *dst0, void *stg0, int64_t W0, int64_t P0,
+                   const void *src1, void *dst1, void *stg1, int64_t W1, int64_t P1,
+                   const void *scale0, void *sdst0, int64_t SW0,
+                   const void *scale1, void *sdst1, int64_t SW1,
+                   int compress, int ctas, int64_t layer, int64_t *seq, int64_t *req,
+                   const int64_t *done, int64_t block, int64_t ring, int64_t retry_ns,
+                   int64_t giveup, uint32_t *scratch, void *stream);
+
 /* ---- decode (subsystem 3) ---- */
 
 /* Replaces decode_rows / _decode_rows_kernel (codec.py:248-327).  For each

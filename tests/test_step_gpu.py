@@ -1,0 +1,110 @@
+"""The fused decode step (xp_decode_step) against the reference's launch sequence.
+
+Two identical pagers (each with its own Store and paging file) take the same
+routing: one through ``LayerPager.decode(fused=True)`` (one launch + one decode
+launch), the other through the reference's sequence (acquire, gather with the
+fused fetch CTA, decode with skip, gather of the SSD misses, decode).  Tables,
+expert_map, slab bytes and SSD statistics must agree after every step, and
+every needed expert's slot must hold its raw rows byte for byte.
+"""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda")
+E, S, W = 32, 8, 8
+
+
+def build(tmp_path, tag, compress, R, experts):
+    from vllm_expert_pager import synthetic
+    from vllm_expert_pager.pager import PARAMS, LayerPager, WorkingSlab
+    from vllm_expert_pager.store import Store
+
+    row_bytes = {n: r * c for n, (r, c) in synthetic.SHAPES.items()}
+    path = str(tmp_path / f"pager-{tag}.bin") if R < E else None
+    store = Store(1, E, R, 2 * W, row_bytes, compress, 0.89, path, DEV)
+    store.retry_ns = 200_000_000
+    for n in PARAMS:
+        q = experts[n][0].cpu()
+        for e in range(E):
+            store.write(0, e, n, q[e])
+    scales = {f"{n[:-7]}_weight_scale": experts[n][1] for n in PARAMS}
+    shapes = {n: (synthetic.SHAPES[n], torch.float8_e4m3fn) for n in PARAMS}
+    all_shapes = dict(shapes)
+    all_shapes.update({k: (tuple(v.shape[1:]), v.dtype) for k, v in scales.items()})
+    return store, LayerPager(store, 0, S, scales, shapes, WorkingSlab(W, all_shapes, store, DEV))
+
+
+@pytest.mark.parametrize("compress,R", [(True, 16), (False, 16), (False, 32), (True, 32)],
+                         ids=["compressed-ssd", "raw-ssd", "raw-ram", "compressed-ram"])
+def test_fused_step_matches_reference_sequence(tmp_path, compress, R):
+    from vllm_expert_pager import synthetic
+    from vllm_expert_pager.pager import PARAMS
+
+    experts = synthetic.fp8_experts_device(E, DEV, seed=4)
+    sa, fused = build(tmp_path, "a", compress, R, experts)
+    sb, ref = build(tmp_path, "b", compress, R, experts)
+    try:
+        g = torch.Generator(device=DEV).manual_seed(9)
+        for step in range(40):
+            k = S if step % 5 else 3
+            ids = torch.randperm(E, generator=g, device=DEV)[:k].to(torch.int32).view(1, -1)
+            ra = fused.decode(ids, fused=True)
+            rb = ref.decode(ids, fused=False)
+            torch.cuda.synchronize()
+            assert torch.equal(ra.expert_map, rb.expert_map), step
+            for t in ("vram", "ram"):
+                for attr in ("slot_of", "expert_in", "last_used", "counters"):
+                    assert torch.equal(getattr(getattr(fused, t), attr),
+                                       getattr(getattr(ref, t), attr)), (step, t, attr)
+            emap = ra.expert_map.cpu()
+            for e in ids.view(-1).tolist():
+                s = int(emap[e])
+                for n in PARAMS:
+                    assert torch.equal(ra.slabs[n][s].view(torch.uint8),
+                                       experts[n][0][e].view(torch.uint8)), (step, e, n)
+                    sn = f"{n[:-7]}_weight_scale"
+                    assert torch.equal(ra.slabs[sn][s], experts[n][1][e])
+        assert fused.step_errors() == 0
+        assert sa.failed is None and sb.failed is None
+        assert (sa.fetches, sa.reads) == (sb.fetches, sb.reads)
+        if R < E:
+            assert sa.reads > 0
+    finally:
+        sa.release()
+        sb.release()
+
+
+def test_fused_step_replays_in_a_cuda_graph(tmp_path):
+    """Captured once (compressed + SSD tier), replayed with new routing each time."""
+    from vllm_expert_pager import synthetic
+    from vllm_expert_pager.pager import PARAMS
+
+    experts = synthetic.fp8_experts_device(E, DEV, seed=5)
+    store, pager = build(tmp_path, "g", True, 16, experts)
+    try:
+        ids = torch.zeros((1, S), dtype=torch.int32, device=DEV)
+        ids.copy_(torch.arange(S, dtype=torch.int32).view(1, -1))
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            pager.decode(ids)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=s):
+                res = pager.decode(ids)
+        torch.cuda.synchronize()
+        g = torch.Generator(device=DEV).manual_seed(1)
+        for _ in range(25):
+            ids.copy_(torch.randperm(E, generator=g, device=DEV)[:S].to(torch.int32).view(1, -1))
+            graph.replay()
+            torch.cuda.synchronize()
+            emap = res.expert_map.cpu()
+            for e in ids.view(-1).tolist():
+                for n in PARAMS:
+                    assert torch.equal(res.slabs[n][int(emap[e])].view(torch.uint8),
+                                       experts[n][0][e].view(torch.uint8))
+        assert pager.step_errors() == 0 and store.failed is None and store.reads > 0
+        del graph
+    finally:
+        store.release()

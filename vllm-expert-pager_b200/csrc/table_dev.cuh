@@ -1,0 +1,178 @@
+// Device functions of the slot-table kernels, shared by table.cu and step.cu.
+//
+// Semantics follow monochromegane/vllm-expert-pager src/vllm_expert_pager/table.py
+// (ExpertTable); citations per function.
+#pragma once
+
+#include <cub/block/block_reduce.cuh>
+#include <cub/block/block_scan.cuh>
+
+#include "common.cuh"
+
+namespace xp {
+namespace tdev {
+
+constexpr int kThreads = 256;
+// Pushes slots whose expert is used this step to the end of the victim order
+// (table.py:14-16).
+constexpr unsigned long long kProtect = 1ull << 40;
+
+using BlockScan = cub::BlockScan<int, kThreads>;
+using BlockReduce = cub::BlockReduce<int, kThreads>;
+
+// Shared memory of one table update.  need/rank are per expert, key/order/evic
+// per slot.
+struct TableSmem {
+  uint8_t *need;              // [E] experts needed this step
+  int *rank;                  // [E] ordinal of a miss, -1 otherwise
+  unsigned long long *key;    // [S] victim key
+  int *order;                 // [S] slots sorted by (key, slot)
+  int *evic;                  // [S] expert evicted by the miss of ordinal r
+};
+
+__host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
+
+__host__ __device__ inline size_t table_smem_bytes(int64_t E, int64_t S) {
+  return align16(E) + align16(4 * E) + 8 * S + align16(4 * S) + align16(4 * S);
+}
+
+__device__ inline TableSmem carve(unsigned char *base, int64_t E, int64_t S) {
+  TableSmem t;
+  unsigned char *p = base;
+  t.key = reinterpret_cast<unsigned long long *>(p);
+  p += 8 * S;
+  t.rank = reinterpret_cast<int *>(p);
+  p += align16(4 * E);
+  t.order = reinterpret_cast<int *>(p);
+  p += align16(4 * S);
+  t.evic = reinterpret_cast<int *>(p);
+  p += align16(4 * S);
+  t.need = p;
+  return t;
+}
+
+struct Table {
+  int64_t *slot_of, *expert_in, *last_used, *counters;
+  int64_t slots;
+};
+
+// need[e] = e occurs in ids[0:K] (table.py:63-71).  Ends with a barrier.
+__device__ inline void build_need(uint8_t *need, const void *ids, int ids_bytes, int64_t K, int64_t E) {
+  for (int64_t e = threadIdx.x; e < E; e += blockDim.x) need[e] = 0;
+  __syncthreads();
+  for (int64_t k = threadIdx.x; k < K; k += blockDim.x) {
+    int64_t id = load_id(ids, ids_bytes, k);
+    if (id >= 0 && id < E) need[id] = 1;
+  }
+  __syncthreads();
+}
+
+// ExpertTable.acquire (table.py:75-128) given the need mask in shared memory.
+//
+// Victims: slots in ascending order of last_used + PROTECT*used, ties by slot
+// number (the stable argsort of table.py:107-108); the miss of ordinal r (misses
+// in ascending expert id, table.py:109) takes the r-th slot of that order.  The
+// slot outputs read slot_of after the update, as the torch version does
+// (table.py:95,118).  Outputs may be null.  count: add hits/misses to the
+// counters (seed restores them, table.py:170-171).
+__device__ inline void acquire_table(const TableSmem &sm, Table t, int64_t E, int64_t K, int32_t *map32,
+                              int64_t *map64, int64_t *slot_out, int64_t *todo, bool count) {
+  const int tid = threadIdx.x;
+  const int64_t S = t.slots;
+  const int64_t step = t.counters[0];
+  __shared__ typename BlockScan::TempStorage scan_tmp;
+  __shared__ typename BlockReduce::TempStorage red_tmp;
+  __shared__ int s_misses, s_hits;
+
+  // Victim keys (table.py:100-107).
+  for (int64_t s = tid; s < S; s += kThreads) {
+    int64_t occ = t.expert_in[s];
+    bool used = occ >= 0 && occ < E && sm.need[occ] && t.slot_of[occ] >= 0;
+    sm.key[s] = static_cast<unsigned long long>(t.last_used[s]) + (used ? kProtect : 0ull);
+  }
+  __syncthreads();
+  // Stable rank of every slot by its key.
+  for (int64_t s = tid; s < S; s += kThreads) {
+    const unsigned long long k = sm.key[s];
+    int pos = 0;
+    for (int64_t u = 0; u < S; ++u) {
+      unsigned long long ku = sm.key[u];
+      pos += (ku < k) | ((ku == k) & (u < s));
+    }
+    sm.order[pos] = static_cast<int>(s);
+  }
+
+  // Hits and misses; miss ordinals by a block-wide scan over experts held in
+  // contiguous ranges per thread (table.py:96-97,109).
+  const int64_t ipt = (E + kThreads - 1) / kThreads;
+  const int64_t e0 = tid * ipt, e1 = e0 + ipt < E ? e0 + ipt : E;
+  int nmiss = 0, nhit = 0;
+  for (int64_t e = e0; e < e1; ++e) {
+    if (sm.need[e]) {
+      if (t.slot_of[e] >= 0) ++nhit;
+      else ++nmiss;
+    }
+  }
+  int base, total;
+  BlockScan(scan_tmp).ExclusiveSum(nmiss, base, total);
+  int hits = BlockReduce(red_tmp).Sum(nhit);
+  if (tid == 0) {
+    s_misses = total;
+    s_hits = hits;
+  }
+  {
+    int r = base;
+    for (int64_t e = e0; e < e1; ++e)
+      sm.rank[e] = (sm.need[e] && t.slot_of[e] < 0) ? r++ : -1;
+  }
+  __syncthreads();  // order[] and rank[] complete
+  const int misses = s_misses;
+  // The expert each victim slot holds now (table.py:113), read before writing.
+  for (int r = tid; r < misses; r += kThreads) {
+    int v = sm.order[r < S ? r : S - 1];
+    sm.evic[r] = static_cast<int>(t.expert_in[v]);
+  }
+  __syncthreads();
+
+  // Update the table (table.py:114-120).  The experts written here are
+  // disjoint: evicted experts are cached and not needed; misses are not cached.
+  for (int64_t e = e0; e < e1; ++e) {
+    if (!sm.need[e]) continue;
+    int r = sm.rank[e];
+    if (r >= 0) {
+      int v = sm.order[r < S ? r : S - 1];
+      int ev = sm.evic[r];
+      if (ev >= 0) t.slot_of[ev] = -1;
+      t.slot_of[e] = v;
+      t.expert_in[v] = e;
+      t.last_used[v] = step;
+    } else {
+      t.last_used[t.slot_of[e]] = step;
+    }
+  }
+  if (todo)
+    for (int64_t k = tid; k < K; k += kThreads) todo[k] = -1;
+  __syncthreads();
+  for (int64_t e = e0; e < e1; ++e) {
+    int r = sm.rank[e];
+    if (todo && r >= 0) todo[r] = e;  // table.py:126-127
+  }
+  for (int64_t e = tid; e < E; e += kThreads) {
+    int64_t s = t.slot_of[e];
+    if (slot_out) slot_out[e] = s;
+    int64_t m = sm.need[e] ? s : -1;  // table.py:125
+    if (map32) map32[e] = static_cast<int32_t>(m);
+    if (map64) map64[e] = m;
+  }
+  if (tid == 0) {
+    t.counters[0] = step + 1;
+    if (count) {
+      t.counters[1] += s_hits;
+      t.counters[2] += misses;
+    }
+  }
+  __syncthreads();
+}
+
+}  // namespace tdev
+}  // namespace xp

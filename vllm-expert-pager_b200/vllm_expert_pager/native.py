@@ -42,6 +42,14 @@ _SIGNATURES = {
     "xp_fetch_publish": (_i32, [_p, _i64, _p, _i64, _i64, _p, _p, _p, _i64, _i64, _p]),
     "xp_fetch_wait": (_i32, [_p, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p]),
     "xp_fetch": (_i32, [_p, _i64, _p, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p]),
+    "xp_decode_step": (_i32, [_p, _i32, _i64, _i64,
+                              _p, _p, _p, _p, _i64, _p, _p, _p,
+                              _p, _p, _p, _p, _i64, _p, _p,
+                              _p, _i64,
+                              _p, _p, _p, _i64, _i64,
+                              _p, _p, _p, _i64, _i64,
+                              _p, _p, _i64, _p, _p, _i64,
+                              _i32, _i32, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _p]),
     "xp_decode_rows": (_i32, [_p, _i64, _p, _p, _p, _p, _i64, _p, _i64, _p, _i64, _p, _i64, _p,
                               _i64, _p]),
     "xp_encode_row": (_i32, [_p, _i64, _i64, _i64, _p, _p, ctypes.POINTER(_i64)]),

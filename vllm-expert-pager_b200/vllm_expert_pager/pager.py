@@ -123,15 +123,25 @@ class LayerPager:
             self.decode_staging = [flat[n][: need[n]].view(S, store.pitch[n]) for n in PARAMS]
         self.ram_view = [store.view[n] for n in PARAMS]
         self.side = torch.cuda.Stream(device=device)
+        # Flags of the fused decode step (zero between launches; word 3 counts
+        # waits that gave up).
+        self.step_scratch = torch.zeros((4,), dtype=torch.int32, device=device)
 
     # ---- decode (experts.py:380-453) ----
 
-    def decode(self, topk_ids: torch.Tensor, gather_events: list | None = None) -> DecodeResult:
+    def decode(self, topk_ids: torch.Tensor, gather_events: list | None = None,
+               fused: bool = True) -> DecodeResult:
         """Page in this step's experts; returns the cache slab and expert_map.
 
-        ``gather_events``: if a list, a (start, end) pair of timing events around
-        the first gather launch is appended (for the benchmark's roofline).
+        ``fused`` (default): one ``xp_decode_step`` launch does the table
+        updates, the RAM copies, the SSD request and wait and the copies of the
+        rows read (plus one decode launch when compressed).  ``fused=False``
+        runs the reference's launch sequence (acquire, gather+fetch, decode,
+        gather, decode).  ``gather_events``: if a list, a (start, end) pair of
+        timing events around the copying launch is appended.
         """
+        if fused:
+            return self._decode_fused(topk_ids, gather_events)
         store, layer = self.store, self.layer
         todo, ssd_todo = self.acquire(topk_ids)
         dst_row, src_row = self.acquire.vram_slot, self.acquire.ram_slot
@@ -159,6 +169,55 @@ class LayerPager:
         if store.compress:
             codec.decode_rows(ssd_todo, dst_row, cached_row, staging, self.cache_bytes, lut)
         return DecodeResult(self.cache_slab, self.expert_map)
+
+    def _decode_fused(self, topk_ids, gather_events=None) -> DecodeResult:
+        from vllm_expert_pager import gather as gather_mod
+        from vllm_expert_pager import native
+        from vllm_expert_pager.table import _ids
+
+        store, layer = self.store, self.layer
+        native.require_cuda(topk_ids)
+        ids, nb = _ids(topk_ids)
+        K = ids.numel()
+        pair, a, b = self.acquire, self.vram, self.ram
+        staging = self.decode_staging
+        st = [t.view(torch.int32) for t in staging] if staging is not None else [None, None]
+        cw, sw = self.cache_rows[:2], self.cache_rows[2:]
+        fetch = store.path is not None
+        if gather_events is not None:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record()
+        native.check(
+            native.lib().xp_decode_step(
+                ids.data_ptr(), nb, K, self.num_experts,
+                *a._table_args(), pair.expert_map.data_ptr(), pair.vram_slot.data_ptr(),
+                pair._vram_todo.data_ptr(),
+                *b._table_args(), pair.ram_slot.data_ptr(), pair._ram_todo.data_ptr(),
+                a.no_cache.data_ptr(), layer * store.ram_slots,
+                self.ram_view[0].data_ptr(), cw[0].data_ptr(), native.ptr(st[0]),
+                cw[0].shape[1], self.ram_view[0].shape[1],
+                self.ram_view[1].data_ptr(), cw[1].data_ptr(), native.ptr(st[1]),
+                cw[1].shape[1], self.ram_view[1].shape[1],
+                self.scale_rows[0].data_ptr(), sw[0].data_ptr(), sw[0].shape[1],
+                self.scale_rows[1].data_ptr(), sw[1].data_ptr(), sw[1].shape[1],
+                int(store.compress), gather_mod.GATHER_CTAS, layer,
+                store.seq.data_ptr() if fetch else None, store.req_dev if fetch else None,
+                store.done_dev if fetch else None, store.block, store.ring, store.retry_ns,
+                store.giveup, self.step_scratch.data_ptr(), native.stream_of(store.device),
+            ),
+            "decode_step",
+        )  # fmt: skip
+        if gather_events is not None:
+            ev[1].record()
+            gather_events.append(ev)
+        if store.compress:
+            codec.decode_rows(pair._vram_todo[:K], pair.vram_slot, a.no_cache, staging,
+                              self.cache_bytes, store.layer_lut(layer))
+        return DecodeResult(self.cache_slab, self.expert_map)
+
+    def step_errors(self) -> int:
+        """Waits of the fused decode step that gave up (host read; not during capture)."""
+        return int(self.step_scratch[3])
 
     # ---- working path (experts.py:455-577) ----
 
