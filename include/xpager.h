@@ -177,6 +177,36 @@ int xp_decode_step(const void *topk_ids, int ids_bytes, int64_t K, int64_t E,
                    const int64_t *done, int64_t block, int64_t ring, int64_t retry_ns,
                    int64_t giveup, uint32_t *scratch, void *stream);
 
+/* Size of the device array xp_decode_step_noalloc takes its scratch from. */
+#define XP_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/* No counterpart in the reference.  For callers that cannot allocate device
+ * memory (an engine that reserved all free memory for its own pools, or a
+ * host that only has this C ABI): xp_decode_step plus, when compressed, the
+ * decode of every VRAM miss (xp_decode_rows with a_todo, a_slot, no_cache,
+ * lut, chunk), with the flag block and the staging rows taken from a fixed
+ * XP_NOALLOC_SCRATCH_BYTES array compiled into the library, held by every GPU
+ * that loads it.  Row sizes W/P are in 32-bit words as in xp_decode_step.
+ * Returns XP_ERANGE (nothing launched) if 256 + K*(P0+P1)*4 staging bytes do
+ * not fit the array.  The first call on a device looks the array up and
+ * clears its flags (synchronous): make it before any stream capture.  All
+ * calls on a device share the array; calls that overlap on the GPU race. */
+int xp_decode_step_noalloc(const void *topk_ids, int ids_bytes, int64_t K, int64_t E,
+                           int64_t *a_slot_of, int64_t *a_expert_in, int64_t *a_last_used,
+                           int64_t *a_counters, int64_t a_slots, int32_t *expert_map,
+                           int64_t *a_slot, int64_t *a_todo,
+                           int64_t *b_slot_of, int64_t *b_expert_in, int64_t *b_last_used,
+                           int64_t *b_counters, int64_t b_slots, int64_t *b_slot, int64_t *b_todo,
+                           const int64_t *no_cache, int64_t base,
+                           const void *src0, void *dst0, int64_t W0, int64_t P0,
+                           const void *src1, void *dst1, int64_t W1, int64_t P1,
+                           const void *scale0, void *sdst0, int64_t SW0,
+                           const void *scale1, void *sdst1, int64_t SW1,
+                           int compress, const uint8_t *lut, int64_t chunk, int ctas,
+                           int64_t layer, int64_t *seq, int64_t *req, const int64_t *done,
+                           int64_t block, int64_t ring, int64_t retry_ns, int64_t giveup,
+                           void *stream);
+
 /* ---- decode (subsystem 3) ---- */
 
 /* Replaces decode_rows / _decode_rows_kernel (codec.py:248-327).  For each

@@ -50,6 +50,15 @@ _SIGNATURES = {
                               _p, _p, _p, _i64, _i64,
                               _p, _p, _i64, _p, _p, _i64,
                               _i32, _i32, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _p]),
+    "xp_decode_step_noalloc": (_i32, [_p, _i32, _i64, _i64,
+                                      _p, _p, _p, _p, _i64, _p, _p, _p,
+                                      _p, _p, _p, _p, _i64, _p, _p,
+                                      _p, _i64,
+                                      _p, _p, _i64, _i64,
+                                      _p, _p, _i64, _i64,
+                                      _p, _p, _i64, _p, _p, _i64,
+                                      _i32, _p, _i64, _i32, _i64, _p, _p, _p, _i64, _i64, _i64,
+                                      _i64, _p]),
     "xp_decode_rows": (_i32, [_p, _i64, _p, _p, _p, _p, _i64, _p, _i64, _p, _i64, _p, _i64, _p,
                               _i64, _p]),
     "xp_encode_row": (_i32, [_p, _i64, _i64, _i64, _p, _p, ctypes.POINTER(_i64)]),
