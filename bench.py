@@ -591,6 +591,78 @@ def run_model_workload(args):
         dist.destroy_process_group()
 
 
+def codec_baselines(device) -> dict:
+    """Config 1 (8 experts, pitch 0.89) on the host cores and on the GPU.
+
+    * ``cpu_encode_port``: the reference's encoder restated in numpy (oracle/),
+      one process -- the reference's own torch encoder cannot run here;
+    * ``cpu_decode_port``: the reference's sequential decoder restated in C
+      (oracle/decode.c) on all host threads;
+    * ``native_encode``: this library's encoder (host, load time), all threads;
+    * ``gpu_decode``: decode_kernel on the same 16 records (8 rows per launch
+      per name, 2 launches).
+    All values are raw MB/s; every round trip is checked byte for byte.
+    """
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle import _lib as olib
+    from oracle import codec as oc
+    from vllm_expert_pager import codec, synthetic
+
+    threads = os.cpu_count() or 1
+    experts = synthetic.fp8_experts(8, seed=0)
+    raws = [synthetic.row_bytes(ex[n][0]).numpy() for ex in experts for n in synthetic.SHAPES]
+    total = sum(r.size for r in raws)
+    t0 = time.perf_counter()
+    recs = [oc.encode(r, oc.pitch_of(r.size, 0.89, 4096)) for r in raws]
+    enc_s = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    for k in (0, 1):  # the w13 rows, then the w2 rows, each batch on all threads
+        rs = [recs[i] for i in range(k, len(recs), 2)]
+        out = olib.decode_rows(np.stack([r[0] for r in rs]), np.stack([r[1] for r in rs]),
+                               raws[k].size, threads=threads)
+        for i, o in zip(range(k, len(recs), 2), out):
+            if not np.array_equal(o, raws[i]):
+                raise SystemExit("oracle decode mismatch")
+    dec_s = time.perf_counter() - t0
+
+    def enc(r):
+        return codec.encode(torch.from_numpy(r), codec.pitch_of(r.size, 0.89, 4096))
+
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(threads) as ex:
+        nat = list(ex.map(enc, raws))
+    nat_s = time.perf_counter() - t0
+    for (a, _, _), (b, _) in zip(recs, nat):
+        if not np.array_equal(a, b.numpy()):
+            raise SystemExit("native encoder differs from the oracle")
+    # GPU: 8 rows per launch per name.
+    lut = torch.zeros((8, 2, 512), dtype=torch.uint8, device=device)
+    stg, dst = [], []
+    for k in (0, 1):
+        rows = [nat[i] for i in range(k, len(nat), 2)]
+        stg.append(torch.stack([r[0] for r in rows]).to(device))
+        dst.append(torch.empty((8, raws[k].size), dtype=torch.uint8, device=device))
+        for e, r in enumerate(rows):
+            lut[e, k] = r[1].to(device)
+    todo = torch.arange(8, dtype=torch.int64, device=device)
+    no_cache = torch.full((8,), -1, dtype=torch.int64, device=device)
+    for _ in range(3):
+        codec.decode_rows(todo, todo, no_cache, stg, dst, lut)
+    gpu_ms = timed(lambda: codec.decode_rows(todo, todo, no_cache, stg, dst, lut), reps=10)
+    for k in (0, 1):
+        for e in range(8):
+            if not np.array_equal(dst[k][e].cpu().numpy(), raws[2 * e + k]):
+                raise SystemExit("gpu decode mismatch")
+    mb = total / 1e6
+    return {"raw_mb": round(mb, 3), "threads": threads,
+            "cpu_encode_port_mb_s": round(mb / enc_s, 1),
+            "cpu_decode_port_mb_s": round(mb / dec_s, 1),
+            "native_encode_mb_s": round(mb / nat_s, 1),
+            "gpu_decode_mb_s": round(mb / (gpu_ms * 1e-3), 1),
+            "record_ratio": round(sum(r[2] for r in recs) / total, 4)}
+
+
 def cpu_port(trace: np.ndarray, steps: int, src_ptrs, slab, threads: int) -> tuple[float, float]:
     """The reference's algorithm on the host: both LRU tables + memcpy of the missed rows.
 
@@ -756,6 +828,7 @@ def main():
                "kind": "port",
                "sample": f"first {sample} of {TRACE_STEPS} trace steps: numpy LRU tables + "
                          f"{threads}-thread memcpy of the missed rows"}
+        cpu["codec_config1"] = codec_baselines(device)
 
     if rank == 0:
         steps_total = args.steps * W

@@ -40,8 +40,10 @@ logger = logging.getLogger(f"vllm.{__name__}")
 # are multiples of this.
 _ALIGN = 4096
 # Threads that read the experts of one layer concurrently (the server itself
-# and the workers), as in the reference (store.py:59-64).
-_READ_WORKERS = 8
+# and the workers): 8 as in the reference (store.py:59-64), which measured an
+# NVMe saturating at 8 outstanding reads.  VLLM_EXPERT_PAGER_READ_WORKERS sets
+# it for devices that want a deeper queue.
+_READ_WORKERS = max(1, int(os.environ.get("VLLM_EXPERT_PAGER_READ_WORKERS", "8")))
 # Slots in the request ring (store.py:65-67).
 RING = 4
 # GPU wait for the host: re-publish every RETRY_NS, give up after GIVEUP
