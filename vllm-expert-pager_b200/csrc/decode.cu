@@ -73,28 +73,51 @@ __device__ __forceinline__ uint32_t spread(uint32_t x) {
   return (t & 0x07070707u) | ((t << 4) & 0x80808080u);
 }
 
-// One symbol for lane state (buf, level): refill (warp-collective), look up,
-// consume.  Returns the LUT entry.  `words` is the group's staged word stream,
-// `rp` the next unread word.
-__device__ __forceinline__ uint32_t step_staged(uint64_t &buf, int &level, int &rp,
-                                                const uint32_t *words, const uint8_t *L1,
-                                                const uint8_t *L, unsigned lt) {
-  const bool need = level < kLimit;
-  const unsigned bal = __ballot_sync(kFull, need);
-  // This lane's word is the popc-th after rp; the mask keeps every read inside
-  // the warp's buffer (a refilling lane of a valid record never leaves its
-  // group's words).
-  const uint32_t w = words[(rp + __popc(bal & lt)) & (kStageWords - 1)];
-  // buf |= w << level as one wide multiply-add (the new bits are above level).
-  const uint32_t mul = need ? (1u << level) : 0u;
-  buf += static_cast<uint64_t>(w) * mul;
-  level += need ? 32 : 0;
-  rp += __popc(bal);
-  uint32_t ent = L1[static_cast<uint32_t>(buf) & 127u];
-  if ((ent & 15u) == 0) ent = L[static_cast<uint32_t>(buf) & (kLutBytes - 1)];
-  const uint32_t len = ent & 15u;
-  buf >>= len;
-  level -= static_cast<int>(len);
+// One symbol step for lane state (buf, level): refill (warp-collective), look
+// up, consume; returns the LUT entry.  Written in PTX, without branches.
+// Shared-memory addresses are 32-bit: words (the staged stream), lut1 (128 B)
+// and lut (512 B); rp4 is the byte offset of the next unread word.  The
+// refilling lanes' word is the popc(bal & lt)-th after rp4 (masked into the
+// warp's buffer: a refilling lane of a valid record never leaves its group's
+// words); buf |= w << level is one wide multiply-add because the new bits lie
+// above level; the 512-byte LUT is read only by lanes whose code is longer
+// than 7 bits (predicated load).
+__device__ __forceinline__ uint32_t step_staged(uint64_t &buf, int &level, uint32_t &rp4,
+                                                uint32_t words, uint32_t lut1, uint32_t lut,
+                                                unsigned lt) {
+  uint32_t ent;
+  asm volatile(
+      "{\n\t"
+      ".reg .pred p, q;\n\t"
+      ".reg .b32 bal, t, c, a, w, m, n, x, len;\n\t"
+      "setp.lt.s32 p, %1, 9;\n\t"
+      "vote.sync.ballot.b32 bal, p, 0xffffffff;\n\t"
+      "and.b32 t, bal, %4;\n\t"
+      "popc.b32 c, t;\n\t"
+      "mad.lo.u32 a, c, 4, %2;\n\t"
+      "and.b32 a, a, %8;\n\t"
+      "add.u32 a, a, %5;\n\t"
+      "ld.shared.u32 w, [a];\n\t"
+      "shl.b32 m, 1, %1;\n\t"
+      "selp.b32 m, m, 0, p;\n\t"
+      "mad.wide.u32 %0, w, m, %0;\n\t"
+      "@p add.s32 %1, %1, 32;\n\t"
+      "popc.b32 n, bal;\n\t"
+      "mad.lo.u32 %2, n, 4, %2;\n\t"
+      "cvt.u32.u64 x, %0;\n\t"
+      "and.b32 t, x, 127;\n\t"
+      "add.u32 t, t, %6;\n\t"
+      "ld.shared.u8 %3, [t];\n\t"
+      "setp.eq.u32 q, %3, 0;\n\t"
+      "and.b32 t, x, 511;\n\t"
+      "add.u32 t, t, %7;\n\t"
+      "@q ld.shared.u8 %3, [t];\n\t"
+      "and.b32 len, %3, 15;\n\t"
+      "shr.b64 %0, %0, len;\n\t"
+      "sub.s32 %1, %1, len;\n\t"
+      "}"
+      : "+l"(buf), "+r"(level), "+r"(rp4), "=r"(ent)
+      : "r"(lt), "r"(words), "r"(lut1), "r"(lut), "n"(4 * kStageWords - 1));
   return ent;
 }
 
@@ -216,7 +239,10 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(const __grid_consta
   const unsigned lt = lanemask_lt();
   uint64_t buf = 0;
   int level = 0;
-  int rp = static_cast<int>(a_begin - a0);
+  uint32_t rp4 = static_cast<uint32_t>(4 * (a_begin - a0));
+  const uint32_t sw = static_cast<uint32_t>(__cvta_generic_to_shared(words));
+  const uint32_t sl1 = static_cast<uint32_t>(__cvta_generic_to_shared(L1));
+  const uint32_t sl = static_cast<uint32_t>(__cvta_generic_to_shared(L));
   const int64_t steps = chunk / 8;
   uint32_t q0 = __ldg(nib + lane);
   uint32_t q1 = steps > 1 ? __ldg(nib + 32 + lane) : 0u;
@@ -230,18 +256,18 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(const __grid_consta
       const uint32_t nw = h ? q1 : q0;
       uint32_t acc_lo, acc_hi;
       {
-        uint32_t ent = step_staged(buf, level, rp, words, L1, L, lt);
+        uint32_t ent = step_staged(buf, level, rp4, sw, sl1, sl, lt);
         acc_lo = ent >> 1;
 #pragma unroll
         for (int k = 1; k < 4; ++k) {
-          ent = step_staged(buf, level, rp, words, L1, L, lt);
+          ent = step_staged(buf, level, rp4, sw, sl1, sl, lt);
           acc_lo += ent << (8 * k - 1);
         }
-        ent = step_staged(buf, level, rp, words, L1, L, lt);
+        ent = step_staged(buf, level, rp4, sw, sl1, sl, lt);
         acc_hi = ent >> 1;
 #pragma unroll
         for (int k = 1; k < 4; ++k) {
-          ent = step_staged(buf, level, rp, words, L1, L, lt);
+          ent = step_staged(buf, level, rp4, sw, sl1, sl, lt);
           acc_hi += ent << (8 * k - 1);
         }
       }
