@@ -591,6 +591,47 @@ def run_model_workload(args):
         dist.destroy_process_group()
 
 
+def bench_acquire(device, steps: int = 1024) -> dict:
+    """Both LRU table updates of a decode step (xp_acquire_pair) on the config-2 trace:
+    device time per launch, and the reference algorithm's port on one host core."""
+    from oracle.table import OracleTable
+    from vllm_expert_pager import synthetic
+    from vllm_expert_pager.acquire import AcquirePair
+    from vllm_expert_pager.table import ExpertTable
+
+    trace = synthetic.zipf_trace(TRACE_STEPS, E, TOPK, 1.1, layer=0)
+    vram, ram = ExpertTable(E, S, device), ExpertTable(E, R, device)
+    ram.slot_of[:R] = ram.experts[:R]
+    ram.expert_in[:R] = ram.experts[:R]
+    pair = AcquirePair(vram, ram)
+    dtrace = trace.to(device)
+    for i in range(64):
+        pair(dtrace[i])
+    # A launch takes a few microseconds on the GPU but longer to enqueue from
+    # Python, so time `steps` launches replayed from one CUDA graph.
+    s = torch.cuda.Stream(device=device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            for i in range(steps):
+                pair(dtrace[64 + i])
+    torch.cuda.synchronize()
+    us = sorted(timed(graph.replay) * 1e3 / steps for _ in range(5))
+    del graph
+    ov, orr = OracleTable(E, S), OracleTable(E, R)
+    orr.warm(R)
+    tr = trace.numpy()
+    t0 = time.perf_counter()
+    for i in range(steps):
+        ov.acquire(tr[i])
+        orr.acquire(tr[i])
+    cpu_us = (time.perf_counter() - t0) / steps * 1e6
+    return {"us_per_launch": round(us[len(us) // 2], 2),
+            "how": f"{steps} launches replayed from a CUDA graph, median of 5 replays",
+            "cpu_port_us_per_step": round(cpu_us, 1), "tables": "VRAM S=32 + RAM R=256, E=256"}
+
+
 def codec_baselines(device) -> dict:
     """Config 1 (8 experts, pitch 0.89) on the host cores and on the GPU.
 
@@ -744,6 +785,7 @@ def main():
     if args.workload == "decode":
         for k in (8, 64):
             print(json.dumps({"decode": bench_decode(device, k)}), flush=True)
+        print(json.dumps({"acquire_pair": bench_acquire(device)}), flush=True)
         return
     if args.ctas:
         gather_mod.GATHER_CTAS = args.ctas
@@ -813,7 +855,8 @@ def main():
     e2e, _, _ = aggregate(e_moved, e_ms, world)
     achieved = moved / (gather_ms * 1e-3) / 1e9 if gather_ms > 0 else None
 
-    kernels = {"decode_k8": bench_decode(device, 8), "decode_k64": bench_decode(device, 64)}
+    kernels = {"decode_k8": bench_decode(device, 8), "decode_k64": bench_decode(device, 64),
+               "acquire_pair": bench_acquire(device)}
 
     cpu = None
     if rank == 0 and world == 1:

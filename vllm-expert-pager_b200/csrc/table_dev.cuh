@@ -20,20 +20,23 @@ constexpr unsigned long long kProtect = 1ull << 40;
 using BlockScan = cub::BlockScan<int, kThreads>;
 using BlockReduce = cub::BlockReduce<int, kThreads>;
 
-// Shared memory of one table update.  need/rank are per expert, key/order/evic
-// per slot.
+// Shared memory of one table update.  Each table is read from global memory
+// once, with coalesced loads, into slot/occ/key; the update then works on
+// these copies and writes back only what changes.
 struct TableSmem {
   uint8_t *need;              // [E] experts needed this step
   int *rank;                  // [E] ordinal of a miss, -1 otherwise
+  int *slot;                  // [E] slot_of (kept up to date through the update)
   unsigned long long *key;    // [S] victim key
   int *order;                 // [S] slots sorted by (key, slot)
   int *evic;                  // [S] expert evicted by the miss of ordinal r
+  int *occ;                   // [S] expert_in before the update
 };
 
 __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
 
 __host__ __device__ inline size_t table_smem_bytes(int64_t E, int64_t S) {
-  return align16(E) + align16(4 * E) + 8 * S + align16(4 * S) + align16(4 * S);
+  return 8 * S + 2 * align16(4 * E) + 3 * align16(4 * S) + align16(E);
 }
 
 __device__ inline TableSmem carve(unsigned char *base, int64_t E, int64_t S) {
@@ -43,9 +46,13 @@ __device__ inline TableSmem carve(unsigned char *base, int64_t E, int64_t S) {
   p += 8 * S;
   t.rank = reinterpret_cast<int *>(p);
   p += align16(4 * E);
+  t.slot = reinterpret_cast<int *>(p);
+  p += align16(4 * E);
   t.order = reinterpret_cast<int *>(p);
   p += align16(4 * S);
   t.evic = reinterpret_cast<int *>(p);
+  p += align16(4 * S);
+  t.occ = reinterpret_cast<int *>(p);
   p += align16(4 * S);
   t.need = p;
   return t;
@@ -75,28 +82,37 @@ __device__ inline void build_need(uint8_t *need, const void *ids, int ids_bytes,
 // slot outputs read slot_of after the update, as the torch version does
 // (table.py:95,118).  Outputs may be null.  count: add hits/misses to the
 // counters (seed restores them, table.py:170-171).
-__device__ inline void acquire_table(const TableSmem &sm, Table t, int64_t E, int64_t K, int32_t *map32,
-                              int64_t *map64, int64_t *slot_out, int64_t *todo, bool count) {
+__device__ inline void acquire_table(const TableSmem &sm, Table t, int64_t E, int64_t K,
+                                     int32_t *map32, int64_t *map64, int64_t *slot_out,
+                                     int64_t *todo, bool count) {
   const int tid = threadIdx.x;
   const int64_t S = t.slots;
-  const int64_t step = t.counters[0];
   __shared__ typename BlockScan::TempStorage scan_tmp;
   __shared__ typename BlockReduce::TempStorage red_tmp;
   __shared__ int s_misses, s_hits;
+  __shared__ long long s_step;
 
-  // Victim keys (table.py:100-107).
+  // One coalesced pass over the table.
+  if (tid == 0) s_step = t.counters[0];
   for (int64_t s = tid; s < S; s += kThreads) {
-    int64_t occ = t.expert_in[s];
-    bool used = occ >= 0 && occ < E && sm.need[occ] && t.slot_of[occ] >= 0;
-    sm.key[s] = static_cast<unsigned long long>(t.last_used[s]) + (used ? kProtect : 0ull);
+    sm.occ[s] = static_cast<int>(t.expert_in[s]);
+    sm.key[s] = static_cast<unsigned long long>(t.last_used[s]);
+  }
+  for (int64_t e = tid; e < E; e += kThreads) sm.slot[e] = static_cast<int>(t.slot_of[e]);
+  __syncthreads();
+  const int64_t step = s_step;
+  // Victim keys: slots whose expert is used this step go last (table.py:100-107).
+  for (int64_t s = tid; s < S; s += kThreads) {
+    const int occ = sm.occ[s];
+    if (occ >= 0 && occ < E && sm.need[occ] && sm.slot[occ] >= 0) sm.key[s] += kProtect;
   }
   __syncthreads();
-  // Stable rank of every slot by its key.
+  // Stable rank of every slot by its key (the stable argsort, table.py:107-108).
   for (int64_t s = tid; s < S; s += kThreads) {
     const unsigned long long k = sm.key[s];
     int pos = 0;
     for (int64_t u = 0; u < S; ++u) {
-      unsigned long long ku = sm.key[u];
+      const unsigned long long ku = sm.key[u];
       pos += (ku < k) | ((ku == k) & (u < s));
     }
     sm.order[pos] = static_cast<int>(s);
@@ -109,58 +125,58 @@ __device__ inline void acquire_table(const TableSmem &sm, Table t, int64_t E, in
   int nmiss = 0, nhit = 0;
   for (int64_t e = e0; e < e1; ++e) {
     if (sm.need[e]) {
-      if (t.slot_of[e] >= 0) ++nhit;
+      if (sm.slot[e] >= 0) ++nhit;
       else ++nmiss;
     }
   }
   int base, total;
   BlockScan(scan_tmp).ExclusiveSum(nmiss, base, total);
-  int hits = BlockReduce(red_tmp).Sum(nhit);
+  const int hits = BlockReduce(red_tmp).Sum(nhit);
   if (tid == 0) {
     s_misses = total;
     s_hits = hits;
   }
   {
     int r = base;
-    for (int64_t e = e0; e < e1; ++e)
-      sm.rank[e] = (sm.need[e] && t.slot_of[e] < 0) ? r++ : -1;
+    for (int64_t e = e0; e < e1; ++e) sm.rank[e] = (sm.need[e] && sm.slot[e] < 0) ? r++ : -1;
   }
   __syncthreads();  // order[] and rank[] complete
   const int misses = s_misses;
-  // The expert each victim slot holds now (table.py:113), read before writing.
-  for (int r = tid; r < misses; r += kThreads) {
-    int v = sm.order[r < S ? r : S - 1];
-    sm.evic[r] = static_cast<int>(t.expert_in[v]);
-  }
+  // The expert each victim slot holds now (table.py:113).
+  for (int r = tid; r < misses; r += kThreads) sm.evic[r] = sm.occ[sm.order[r < S ? r : S - 1]];
   __syncthreads();
 
   // Update the table (table.py:114-120).  The experts written here are
   // disjoint: evicted experts are cached and not needed; misses are not cached.
   for (int64_t e = e0; e < e1; ++e) {
     if (!sm.need[e]) continue;
-    int r = sm.rank[e];
+    const int r = sm.rank[e];
     if (r >= 0) {
-      int v = sm.order[r < S ? r : S - 1];
-      int ev = sm.evic[r];
-      if (ev >= 0) t.slot_of[ev] = -1;
+      const int v = sm.order[r < S ? r : S - 1];
+      const int ev = sm.evic[r];
+      if (ev >= 0) {
+        t.slot_of[ev] = -1;
+        sm.slot[ev] = -1;
+      }
       t.slot_of[e] = v;
+      sm.slot[e] = v;
       t.expert_in[v] = e;
       t.last_used[v] = step;
     } else {
-      t.last_used[t.slot_of[e]] = step;
+      t.last_used[sm.slot[e]] = step;
     }
   }
   if (todo)
     for (int64_t k = tid; k < K; k += kThreads) todo[k] = -1;
   __syncthreads();
   for (int64_t e = e0; e < e1; ++e) {
-    int r = sm.rank[e];
+    const int r = sm.rank[e];
     if (todo && r >= 0) todo[r] = e;  // table.py:126-127
   }
   for (int64_t e = tid; e < E; e += kThreads) {
-    int64_t s = t.slot_of[e];
+    const int64_t s = sm.slot[e];  // slot_of after the update (table.py:95,118)
     if (slot_out) slot_out[e] = s;
-    int64_t m = sm.need[e] ? s : -1;  // table.py:125
+    const int64_t m = sm.need[e] ? s : -1;  // table.py:125
     if (map32) map32[e] = static_cast<int32_t>(m);
     if (map64) map64[e] = m;
   }
