@@ -27,6 +27,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import select
 import statistics
 import subprocess
 import sys
@@ -53,10 +54,13 @@ def parse():
     p.add_argument("--window", type=int, default=512)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--ctas", type=int, default=0, help="gather CTAs (0 = library default)")
-    p.add_argument("--workload", choices=["paging", "decode", "model", "compressed", "prefill"],
+    p.add_argument("--workload", choices=["paging", "decode", "model", "compressed", "prefill",
+                                          "reference-triton"],
                    default="paging",
                    help="paging: config 2 (the headline line); decode: the decode kernel alone; "
-                        "model/compressed/prefill: configs 3/4/5 on a paged 40-layer MoE")
+                        "model/compressed/prefill: configs 3/4/5 on a paged 40-layer MoE; "
+                        "reference-triton: the reference's own Triton kernels from baseline/_ref "
+                        "on the inputs of paging/decode (one GPU)")
     p.add_argument("--layers", type=int, default=40, help="MoE layers of configs 3-5")
     p.add_argument("--tokens", type=int, default=512, help="decode tokens of configs 3-4")
     return p.parse_args()
@@ -135,6 +139,12 @@ class Clocks:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return self
+        # nvidia-smi takes a moment to start: wait for its first (idle, discarded)
+        # sample so that a short timed region still gets sampled.
+        ready, _, _ = select.select([self.proc.stdout], [], [], 10.0)
+        if ready:
+            self.proc.stdout.readline()
         return self
 
     def __exit__(self, *a):
@@ -189,13 +199,19 @@ def build_workload(device: torch.device):
     return store, pager, trace
 
 
-def measure_h2d_peak(device) -> float:
-    """Copy-engine pinned->device bandwidth (GB/s), 1 GiB, best of 5."""
+def measure_h2d_peak(device, world: int = 1) -> float:
+    """Copy-engine pinned->device bandwidth (GB/s), 1 GiB, best of 6.
+
+    With several ranks every rank copies at the same time (a barrier before each
+    copy), so the figure is one replica's share of the host links and host memory
+    while all replicas page, which is the bench's own load.
+    """
     n = 1 << 30
     src = torch.empty(n, dtype=torch.uint8, pin_memory=True)
     dst = torch.empty(n, dtype=torch.uint8, device=device)
     best = 0.0
     for _ in range(6):
+        barrier(world)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         dst.copy_(src, non_blocking=True)
@@ -729,6 +745,189 @@ def cpu_port(trace: np.ndarray, steps: int, src_ptrs, slab, threads: int) -> tup
     return time.perf_counter() - t0, moved
 
 
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def _synthetic_by_path():
+    """This repository's seeded generators (synthetic.py imports only torch), loaded by
+    file so that the name ``vllm_expert_pager`` stays free for the reference install."""
+    import importlib.util
+
+    path = os.path.join(ROOT, "vllm-expert-pager_b200", "vllm_expert_pager", "synthetic.py")
+    spec = importlib.util.spec_from_file_location("xp_synthetic", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def run_reference_triton(args) -> None:
+    """The reference's own GPU kernels (Triton, installed unmodified in baseline/_ref) on
+    this GPU, on the inputs this bench gives its own kernels.
+
+    * ``acquire_pair``: ``AcquirePair`` on the config-2 trace, 1024 launches replayed
+      from a CUDA graph (as ``bench_acquire``);
+    * ``decode_step_config2``: the stock decode step of ``forward_modular`` with an
+      uncompressed RAM tier holding every expert -- ``AcquirePair``, ``gather_rows`` of
+      the VRAM misses, ``gather_rows`` of the (empty) SSD list -- one CUDA graph per
+      window of ``--window`` trace steps; GB/s = misses x 3 MiB / device time.  The
+      first gather runs without ``fetch=``: with every expert in RAM the SSD list is
+      empty and ``fetch=`` only adds a program that publishes nothing;
+    * ``decode_k8`` / ``decode_k64``: ``decode_rows`` on config-1 records made by the
+      reference's ``codec.encode`` (pitch 0.89), as ``bench_decode``.
+    """
+    line = {"impl": "reference", "workload": "reference-triton"}
+    if not os.path.isdir(os.path.join(REF_DIR, "vllm_expert_pager")):
+        line["unavailable"] = "baseline/_ref holds no install of the reference"
+        print(json.dumps(line), flush=True)
+        return
+    sys.path.insert(0, REF_DIR)
+    import vllm_expert_pager as refpkg
+
+    if not os.path.abspath(refpkg.__file__).startswith(REF_DIR):
+        raise SystemExit("vllm_expert_pager did not resolve to baseline/_ref")
+    from vllm_expert_pager import codec as rcodec
+    from vllm_expert_pager.acquire import AcquirePair
+    from vllm_expert_pager.gather import as_rows, gather_rows
+    from vllm_expert_pager.table import ExpertTable
+
+    syn = _synthetic_by_path()
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    trace = syn.zipf_trace(TRACE_STEPS, E, TOPK, 1.1, layer=0)
+    dtrace = trace.to(device)
+
+    def tables():
+        vram, ram = ExpertTable(E, S, device), ExpertTable(E, R, device)
+        ram.slot_of[:R] = ram.experts[:R]
+        ram.expert_in[:R] = ram.experts[:R]
+        return vram, ram, AcquirePair(vram, ram)
+
+    # acquire_pair
+    vram, ram, pair = tables()
+    for i in range(64):
+        pair(dtrace[i])
+    steps = 1024
+    s = torch.cuda.Stream(device=device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            for i in range(steps):
+                pair(dtrace[64 + i])
+    torch.cuda.synchronize()
+    us = sorted(timed(graph.replay) * 1e3 / steps for _ in range(5))
+    del graph
+    kernels = {"acquire_pair": {"us_per_launch": round(us[len(us) // 2], 2),
+                                "how": f"{steps} launches replayed from a CUDA graph, "
+                                       "median of 5 replays"}}
+
+    # decode step, config 2
+    row = {n: r * c for n, (r, c) in syn.SHAPES.items()}
+    src = [as_rows(torch.zeros((E, b), dtype=torch.uint8).pin_memory()) for b in row.values()]
+    slab = [torch.zeros((S, b // 4), dtype=torch.int32, device=device) for b in row.values()]
+    sw = [(r // 128) * (c // 128) for r, c in syn.SHAPES.values()]
+    scale = [torch.zeros((E, w), dtype=torch.int32, device=device) for w in sw]
+    scale_dst = [torch.zeros((S, w), dtype=torch.int32, device=device) for w in sw]
+    vram, ram, pair = tables()
+
+    def step(ids):
+        todo, ssd = pair(ids)
+        gather_rows(todo, pair.vram_slot, vram.no_cache, pair.ram_slot, 0, src, slab, slab,
+                    None, scale, scale_dst)
+        gather_rows(ssd, pair.vram_slot, vram.no_cache, pair.ram_slot, 0, src, slab, slab,
+                    None, scale, scale_dst)
+
+    W = args.window
+    pos = 0
+    for _ in range(args.warmup):
+        for i in range(W):
+            step(dtrace[(pos + i) % TRACE_STEPS])
+        pos += W
+    torch.cuda.synchronize()
+    graphs = []
+    for _ in range(args.steps):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                for i in range(W):
+                    step(dtrace[(pos + i) % TRACE_STEPS])
+        graphs.append(g)
+        pos += W
+    torch.cuda.synchronize()
+    # Capture records the kernels without running them: the tables are where the
+    # warm-up left them, and the replays below walk the captured windows in order.
+    miss0 = int(vram.misses)
+
+    def replay_all():
+        for g in graphs:
+            g.replay()
+
+    ms = timed(replay_all)
+    moved = (int(vram.misses) - miss0) * EXPERT_BYTES
+    del graphs
+    kernels["decode_step_config2"] = {
+        "value": round(moved / (ms * 1e-3) / 1e9, 3), "unit": "GB/s",
+        "ms_per_window": round(ms / args.steps, 3), "window": W, "windows": args.steps,
+        "launches_per_step": 3, "how": "one CUDA graph per window, replayed back to back"}
+    del src
+
+    # decode_rows, config-1 records
+    names = list(syn.SHAPES)
+    gen = torch.Generator().manual_seed(0)
+    experts = [syn.fp8_expert(gen) for _ in range(8)]
+    distinct = 64
+    raws = {n: [syn.row_bytes(ex[n][0]) for ex in experts] for n in names}
+    enc = {n: [rcodec.encode(r.to(device), rcodec.pitch_of(r.numel(), 0.89, 4096))
+               for r in raws[n]] for n in names}
+    used = 0
+    for n in names:
+        for (rec, _), r in zip(enc[n], raws[n]):
+            G = r.numel() // (rcodec.CHUNK * rcodec.LANES)
+            used += 4 * (G + 1) + r.numel() // 2 + 4 * int(rec[4 * G : 4 * G + 4].view(torch.int32))
+    per_row = used / 8 + sum(raws[n][0].numel() for n in names) + 2 * 512
+    stg = [torch.stack([enc[n][e % 8][0] for e in range(distinct)]) for n in names]
+    dst = [torch.empty((distinct, raws[n][0].numel()), dtype=torch.uint8, device=device)
+           for n in names]
+    lut = torch.stack([torch.stack([enc[n][e % 8][1] for n in names])
+                       for e in range(distinct)]).to(device)
+    ident = torch.arange(distinct, dtype=torch.int64, device=device)
+    no_cache = torch.full((distinct,), -1, dtype=torch.int64, device=device)
+    peak, psrc = hbm_peak()
+    for K in (8, 64):
+        starts = list(range(0, distinct - K + 1, K))
+        todos = [torch.arange(s0, s0 + K, dtype=torch.int64, device=device) for s0 in starts]
+
+        def launch(i):
+            s0 = starts[i % len(starts)]
+            rcodec.decode_rows(todos[i % len(starts)], ident, no_cache,
+                               [x[s0 : s0 + K] for x in stg], dst, lut)
+
+        for i in range(4):
+            launch(i)
+        torch.cuda.synchronize()
+        best = None
+        for _ in range(3):
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(24)]
+            for i in range(24):
+                ev[i][0].record()
+                launch(i)
+                ev[i][1].record()
+            torch.cuda.synchronize()
+            t = sum(a.elapsed_time(b) for a, b in ev) * 1e3 / 24
+            best = t if best is None else min(best, t)
+        for n, d in zip(names, dst):
+            if not torch.equal(d[K - 1].cpu(), raws[n][(K - 1) % 8]):
+                raise SystemExit(f"reference decode mismatch ({n})")
+        achieved = K * per_row / (best * 1e-6) / 1e9
+        kernels[f"decode_k{K}"] = {"rows_per_launch": K, "us_per_launch": round(best, 2),
+                                   "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                                   "frac": round(achieved / peak, 4), "peak_source": psrc}
+    line["kernels"] = kernels
+    line["device"] = torch.cuda.get_device_name(device)
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args, world, rank):
     """--impl reference: the CPU restatement of the reference path on the host cores."""
     if rank != 0:
@@ -772,6 +971,10 @@ def run_reference(args, world, rank):
 
 def main():
     args = parse()
+    if args.workload == "reference-triton":
+        if int(os.environ.get("RANK", "0")) == 0:
+            run_reference_triton(args)
+        return
     if args.workload in ("model", "compressed", "prefill"):
         run_model_workload(args)
         return
@@ -792,7 +995,7 @@ def main():
     store, pager, trace_cpu = build_workload(device)
     trace = trace_cpu.to(device)
     W = args.window
-    peak = measure_h2d_peak(device)
+    peak = measure_h2d_peak(device, world)
 
     def window(w0: int, events=None):
         for i in range(W):
@@ -895,8 +1098,10 @@ def main():
                          "kernel": "step_kernel (both table updates + the gather, one launch "
                                    "per decode step)",
                          "peak_source": "measured in bench.py: copy engine pinned->device, "
-                                        "1 GiB, best of 6 (MEASURED_PEAKS.json has no host-link "
-                                        "figure)"},
+                                        "1 GiB, best of 6" + (
+                                            f", all {world} ranks copying at once"
+                                            if world > 1 else "") +
+                                        " (MEASURED_PEAKS.json has no host-link figure)"},
             "kernels": kernels,
             "gpu_launches": args.steps * W,
             "cpu_baseline": cpu,

@@ -73,6 +73,56 @@ def test_random_distributions_match_oracle(seed):
     assert np.array_equal(a, raw)
 
 
+def _canonical(lut: np.ndarray) -> bool:
+    """The decoder's fast-path rule: each window's code length is 1 + the number of
+    thresholds lim[L] (windows with codes of at most L bits) that the window, read
+    most-significant bit first, reaches."""
+    lens = lut.astype(np.int64) & 15
+    lim = [(lens <= L).sum() for L in range(1, 9)]
+    r = np.array([int(format(x, "09b")[::-1], 2) for x in range(512)])
+    return bool(((lens >= 1) & (lens == 1 + sum((r >= t).astype(np.int64) for t in lim))).all())
+
+
+def _complemented(rec: np.ndarray, lut: np.ndarray, n: int, chunk: int):
+    """The same row under the bit-complemented code: every Huffman word inverted,
+    lut'[x] = lut[x ^ 511].  Prefix-free, complete and with the same lengths (so
+    the same refills), but longer codes come first: not canonical."""
+    G = n // (chunk * 32)
+    head = 4 * (G + 1) + n // 2
+    end = head + 4 * int(rec[: 4 * (G + 1)].view(np.uint32)[-1])
+    out = rec.copy()
+    out[head:end] ^= 0xFF
+    return out, lut[np.arange(512) ^ 511].copy()
+
+
+@pytest.mark.parametrize("chunk", [64, 512])
+def test_non_canonical_lut_decodes_through_the_table(chunk):
+    """A valid but non-canonical code takes the LUT-chain step and still matches."""
+    n = 32 * chunk * 3
+    p = np.random.default_rng(11).dirichlet(np.full(16, 0.3))
+    raw = rows(11, n, p.tolist()).numpy()
+    rec, lut, _ = oc.encode(raw, oc.pitch_of(n, 1.5, 4096) + 4096, chunk)
+    rec2, lut2 = _complemented(rec, lut, n, chunk)
+    assert _canonical(lut) and not _canonical(lut2)
+    a, _ = decode_one(rec2, lut2, n, chunk)
+    assert np.array_equal(a, oracle_lib.decode(rec2, lut2, n, chunk))
+    assert np.array_equal(a, raw)
+
+
+def test_relabelled_symbols_come_from_the_lut():
+    """Permuting the LUT's symbols keeps the code canonical; the bytes follow the LUT."""
+    n = 32 * 512 * 2
+    raw = rows(12, n).numpy()
+    rec, lut, _ = oc.encode(raw, oc.pitch_of(n, 1.5, 4096) + 4096, 512)
+    perm = np.random.default_rng(12).permutation(16)
+    lut2 = ((perm[lut >> 4] << 4) | (lut & 15)).astype(np.uint8)
+    assert _canonical(lut2)
+    a, _ = decode_one(rec, lut2, n, 512)
+    want = (raw & 0x87) | (perm[(raw >> 3) & 15] << 3).astype(np.uint8)
+    assert np.array_equal(a, oracle_lib.decode(rec, lut2, n, 512))
+    assert np.array_equal(a, want)
+
+
 def test_decode_rows_follows_todo_and_skips():
     """The reference test_codec.py::test_decode_rows_follows_todo_and_skips, at CHUNK=64."""
     from vllm_expert_pager import codec

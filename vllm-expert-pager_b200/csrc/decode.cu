@@ -244,10 +244,14 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(const __grid_consta
   const uint32_t sl1 = static_cast<uint32_t>(__cvta_generic_to_shared(L1));
   const uint32_t sl = static_cast<uint32_t>(__cvta_generic_to_shared(L));
   const int64_t steps = chunk / 8;
+  // Nibble words are prefetched two iterations ahead.  The index is clamped
+  // (steps is even and at least 2) rather than the load predicated, so that no
+  // select consumes a load right after it is issued.
+  const int64_t last = steps - 1;
   uint32_t q0 = __ldg(nib + lane);
-  uint32_t q1 = steps > 1 ? __ldg(nib + 32 + lane) : 0u;
-  uint32_t q2 = steps > 2 ? __ldg(nib + 64 + lane) : 0u;
-  uint32_t q3 = steps > 3 ? __ldg(nib + 96 + lane) : 0u;
+  uint32_t q1 = __ldg(nib + 32 + lane);
+  uint32_t q2 = __ldg(nib + (2 < last ? 2 : last) * 32 + lane);
+  uint32_t q3 = __ldg(nib + (3 < last ? 3 : last) * 32 + lane);
   uint4 *out = reinterpret_cast<uint4 *>(out_row);
   for (int64_t m = 0; m < steps; m += 2) {
     uint32_t lohi[4];
@@ -277,8 +281,8 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(const __grid_consta
     out[m / 2] = make_uint4(lohi[0], lohi[1], lohi[2], lohi[3]);
     q0 = q2;
     q1 = q3;
-    q2 = m + 4 < steps ? __ldg(nib + (m + 4) * 32 + lane) : 0u;
-    q3 = m + 5 < steps ? __ldg(nib + (m + 5) * 32 + lane) : 0u;
+    q2 = __ldg(nib + (m + 4 < last ? m + 4 : last) * 32 + lane);
+    q3 = __ldg(nib + (m + 5 < last ? m + 5 : last) * 32 + lane);
   }
 }
 

@@ -93,11 +93,13 @@ __global__ void __launch_bounds__(gdev::kThreads) step_kernel(const __grid_const
   if (role < 2) {
     const int64_t S = p.a.slots > p.b.slots ? p.a.slots : p.b.slots;
     TableSmem sm = tdev::carve(smem, p.E, S);
-    tdev::build_need(sm.need, p.ids, p.ids_bytes, p.K, p.E);
-    if (role == 0)
-      tdev::acquire_table(sm, p.a, p.E, p.K, p.map32, nullptr, p.a_slot, p.a_todo, true);
-    else
-      tdev::acquire_table(sm, p.b, p.E, p.K, nullptr, nullptr, p.b_slot, p.b_todo, true);
+    if (role == 0) {
+      tdev::need_and_table(sm, p.a, p.ids, p.ids_bytes, p.K, p.E);
+      tdev::acquire_table(sm, p.a, p.E, p.K, p.map32, nullptr, p.a_slot, p.a_todo, true, true);
+    } else {
+      tdev::need_and_table(sm, p.b, p.ids, p.ids_bytes, p.K, p.E);
+      tdev::acquire_table(sm, p.b, p.E, p.K, nullptr, nullptr, p.b_slot, p.b_todo, true, true);
+    }
     raise_flag(&flags[0]);
   } else if (p.fetch && role == static_cast<int>(gridDim.x) - 1) {
     if (wait_flag(&flags[0], 2, p.table_wait_ns, &flags[3])) {

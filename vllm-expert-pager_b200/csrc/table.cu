@@ -28,11 +28,13 @@ __global__ void __launch_bounds__(kThreads) acquire_pair_kernel(const __grid_con
   extern __shared__ __align__(16) unsigned char smem[];
   const int64_t S = p.a.slots > p.b.slots ? p.a.slots : p.b.slots;
   TableSmem sm = carve(smem, p.E, S);
-  build_need(sm.need, p.ids, p.ids_bytes, p.K, p.E);
-  if (blockIdx.x == 0)
-    acquire_table(sm, p.a, p.E, p.K, p.map32, nullptr, p.a_slot, p.a_todo, true);
-  else
-    acquire_table(sm, p.b, p.E, p.K, nullptr, nullptr, p.b_slot, p.b_todo, true);
+  if (blockIdx.x == 0) {
+    need_and_table(sm, p.a, p.ids, p.ids_bytes, p.K, p.E);
+    acquire_table(sm, p.a, p.E, p.K, p.map32, nullptr, p.a_slot, p.a_todo, true, true);
+  } else {
+    need_and_table(sm, p.b, p.ids, p.ids_bytes, p.K, p.E);
+    acquire_table(sm, p.b, p.E, p.K, nullptr, nullptr, p.b_slot, p.b_todo, true, true);
+  }
 }
 
 struct OneArgs {
@@ -46,8 +48,8 @@ struct OneArgs {
 __global__ void __launch_bounds__(kThreads) acquire_kernel(const __grid_constant__ OneArgs p) {
   extern __shared__ __align__(16) unsigned char smem[];
   TableSmem sm = carve(smem, p.E, p.t.slots);
-  build_need(sm.need, p.ids, p.ids_bytes, p.K, p.E);
-  acquire_table(sm, p.t, p.E, p.K, nullptr, p.map64, p.slot, p.todo, true);
+  need_and_table(sm, p.t, p.ids, p.ids_bytes, p.K, p.E);
+  acquire_table(sm, p.t, p.E, p.K, nullptr, p.map64, p.slot, p.todo, true, true);
 }
 
 __global__ void need_mask_kernel(const void *ids, int ids_bytes, int64_t K, int64_t E,
@@ -127,7 +129,7 @@ __global__ void __launch_bounds__(kThreads) seed_kernel(const __grid_constant__ 
     __syncthreads();
     for (int64_t i = tid; i < ntop; i += kThreads) sm.need[top[i]] = 1;
     __syncthreads();
-    acquire_table(sm, p.t, E, ntop, nullptr, nullptr, nullptr, nullptr, false);
+    acquire_table(sm, p.t, E, ntop, nullptr, nullptr, nullptr, nullptr, false, false);
   }
   // The VRAM tier's experts that are in the RAM table or referenced
   // (table.py:167-169).
@@ -139,7 +141,7 @@ __global__ void __launch_bounds__(kThreads) seed_kernel(const __grid_constant__ 
     sm.need[ok ? v : top0] = 1;
   }
   __syncthreads();
-  acquire_table(sm, p.t, E, S, nullptr, nullptr, nullptr, nullptr, false);
+  acquire_table(sm, p.t, E, S, nullptr, nullptr, nullptr, nullptr, false, false);
 }
 
 struct PlanArgs {
