@@ -745,6 +745,34 @@ def cpu_port(trace: np.ndarray, steps: int, src_ptrs, slab, threads: int) -> tup
     return time.perf_counter() - t0, moved
 
 
+def time_planning(table_cls, syn, device, layers: int = 40, reps: int = 3) -> dict:
+    """Working-path planning of one layer at config 5 (2048-token prefill, uniform top-8,
+    E=256, S=32, R=128, W=64): ``need_mask``, the ``slot_of`` copy, ``seed`` and
+    ``plan_chunks``, issued eagerly as ``_expert_pager_forward_working`` issues them
+    (experts.py:500-511).  ``table_cls`` is this library's ``ExpertTable`` or the
+    reference's (same methods); device time from the first launch to the last, host
+    issue included, per layer."""
+    e_, s_, r_, w_ = 256, 32, 128, 64
+    ids = syn.uniform_routing(2048, e_, 8, seed=0).to(device)
+    vram, ram = table_cls(e_, s_, device), table_cls(e_, r_, device)
+    warm = syn.zipf_trace(64, e_, 8, 1.1, layer=0).to(device)
+    for i in range(64):
+        vram.acquire(warm[i])
+
+    def plan():
+        need = ram.need_mask(ids)
+        before = ram.slot_of[:e_].clone()
+        ram.seed(vram, ids, need)
+        ram.plan_chunks(before, need, vram.slot_of[:e_], w_, 0, 40 * r_)
+
+    for _ in range(3):
+        plan()
+    torch.cuda.synchronize()
+    best = min(timed(lambda: [plan() for _ in range(layers)]) / layers for _ in range(reps))
+    return {"ms_per_layer": round(best, 4),
+            "how": f"{layers} layers back to back, eager, best of {reps}"}
+
+
 REF_DIR = os.path.join(ROOT, "baseline", "_ref")
 
 
@@ -923,6 +951,7 @@ def run_reference_triton(args) -> None:
         kernels[f"decode_k{K}"] = {"rows_per_launch": K, "us_per_launch": round(best, 2),
                                    "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                                    "frac": round(achieved / peak, 4), "peak_source": psrc}
+    kernels["plan_config5"] = time_planning(ExpertTable, syn, device)
     line["kernels"] = kernels
     line["device"] = torch.cuda.get_device_name(device)
     print(json.dumps(line), flush=True)
@@ -989,6 +1018,11 @@ def main():
         for k in (8, 64):
             print(json.dumps({"decode": bench_decode(device, k)}), flush=True)
         print(json.dumps({"acquire_pair": bench_acquire(device)}), flush=True)
+        from vllm_expert_pager import synthetic
+        from vllm_expert_pager.table import ExpertTable
+
+        print(json.dumps({"plan_config5": time_planning(ExpertTable, synthetic, device)}),
+              flush=True)
         return
     if args.ctas:
         gather_mod.GATHER_CTAS = args.ctas

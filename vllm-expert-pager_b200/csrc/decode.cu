@@ -34,7 +34,9 @@ namespace {
 constexpr int kWarps = 4;
 constexpr int kLimit = 9;
 constexpr int kLutBytes = 512;
-constexpr int kStageWords = 2048;  // per-warp shared buffer for a group's Huffman words
+// Per-warp shared buffer for a group's Huffman words, in words: sized per launch
+// from the records' pitch (see stage_words_for), within these bounds.
+constexpr int64_t kStageMin = 1024, kStageMax = 4096;
 constexpr unsigned kFull = 0xffffffffu;
 
 struct DName {
@@ -53,6 +55,7 @@ struct DecodeArgs {
   DName n[2];
   const int64_t *skip;
   int64_t chunk;
+  int64_t stage_words;  // per-warp word buffer (multiple of 4)
 };
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem, int src_bytes) {
@@ -75,15 +78,16 @@ __device__ __forceinline__ uint32_t spread(uint32_t x) {
 
 // One symbol step for lane state (buf, level): refill (warp-collective), look
 // up, consume; returns the LUT entry.  Written in PTX, without branches.
-// Shared-memory addresses are 32-bit: words (the staged stream), lut1 (128 B)
-// and lut (512 B); rp4 is the byte offset of the next unread word.  The
-// refilling lanes' word is the popc(bal & lt)-th after rp4 (masked into the
-// warp's buffer: a refilling lane of a valid record never leaves its group's
-// words); buf |= w << level is one wide multiply-add because the new bits lie
-// above level; the 512-byte LUT is read only by lanes whose code is longer
-// than 7 bits (predicated load).
-__device__ __forceinline__ uint32_t step_staged(uint64_t &buf, int &level, uint32_t &rp4,
-                                                uint32_t words, uint32_t lut1, uint32_t lut,
+// Shared-memory addresses are 32-bit: rp (the next unread word of the staged
+// stream), lut1 (128 B) and lut (512 B).  The refilling lanes' word is the
+// popc(bal & lt)-th after rp; rp is clamped to cap after each advance, off the
+// symbol-to-symbol chain, so that rp + 4 * 31 stays inside the warp's buffer
+// (a refilling lane of a valid record never leaves its group's words, which
+// end at least 32 words before the buffer's end); buf |= w << level is one wide
+// multiply-add because the new bits lie above level; the 512-byte LUT is read
+// only by lanes whose code is longer than 7 bits (predicated load).
+__device__ __forceinline__ uint32_t step_staged(uint64_t &buf, int &level, uint32_t &rp,
+                                                uint32_t cap, uint32_t lut1, uint32_t lut,
                                                 unsigned lt) {
   uint32_t ent;
   asm volatile(
@@ -95,8 +99,6 @@ __device__ __forceinline__ uint32_t step_staged(uint64_t &buf, int &level, uint3
       "and.b32 t, bal, %4;\n\t"
       "popc.b32 c, t;\n\t"
       "mad.lo.u32 a, c, 4, %2;\n\t"
-      "and.b32 a, a, %8;\n\t"
-      "add.u32 a, a, %5;\n\t"
       "ld.shared.u32 w, [a];\n\t"
       "shl.b32 m, 1, %1;\n\t"
       "selp.b32 m, m, 0, p;\n\t"
@@ -104,6 +106,7 @@ __device__ __forceinline__ uint32_t step_staged(uint64_t &buf, int &level, uint3
       "@p add.s32 %1, %1, 32;\n\t"
       "popc.b32 n, bal;\n\t"
       "mad.lo.u32 %2, n, 4, %2;\n\t"
+      "min.u32 %2, %2, %5;\n\t"
       "cvt.u32.u64 x, %0;\n\t"
       "and.b32 t, x, 127;\n\t"
       "add.u32 t, t, %6;\n\t"
@@ -116,8 +119,8 @@ __device__ __forceinline__ uint32_t step_staged(uint64_t &buf, int &level, uint3
       "shr.b64 %0, %0, len;\n\t"
       "sub.s32 %1, %1, len;\n\t"
       "}"
-      : "+l"(buf), "+r"(level), "+r"(rp4), "=r"(ent)
-      : "r"(lt), "r"(words), "r"(lut1), "r"(lut), "n"(4 * kStageWords - 1));
+      : "+l"(buf), "+r"(level), "+r"(rp), "=r"(ent)
+      : "r"(lt), "r"(cap), "r"(lut1), "r"(lut));
   return ent;
 }
 
@@ -173,7 +176,7 @@ __device__ void decode_group_window(const uint32_t *huff, int64_t wbase, int64_t
 }
 
 __global__ void __launch_bounds__(kWarps * 32) decode_kernel(const __grid_constant__ DecodeArgs a) {
-  __shared__ __align__(16) uint32_t s_words[kWarps][kStageWords];
+  extern __shared__ __align__(16) uint32_t s_words[];  // [kWarps][stage_words]
   __shared__ __align__(16) uint8_t s_lut[kWarps][kLutBytes];
   __shared__ __align__(16) uint8_t s_lut1[kWarps][128];
   const int64_t j = blockIdx.y;
@@ -219,14 +222,14 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(const __grid_consta
   const int64_t a_begin = huff_w + w_begin, a_end = huff_w + w_end;
   const int64_t a0 = a_begin & ~int64_t(3);
   const int64_t units = (a_end - a0 + 3) / 4;
-  const bool staged = units * 4 <= kStageWords && (chunk / 8) % 2 == 0;
+  const bool staged = units * 4 + 32 <= a.stage_words && (chunk / 8) % 2 == 0;
   if (!staged) {
     __syncwarp();
     decode_group_window(reinterpret_cast<const uint32_t *>(rec) + huff_w, w_begin,
                         w_end, nib, out_row, chunk, L1, L, lane);
     return;
   }
-  uint32_t *words = s_words[warp];
+  uint32_t *words = s_words + warp * a.stage_words;
   for (int64_t u = lane; u < units; u += 32) {
     const int64_t w = a0 + 4 * u;
     int64_t bytes = (rec_w - w) * 4;
@@ -239,8 +242,9 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(const __grid_consta
   const unsigned lt = lanemask_lt();
   uint64_t buf = 0;
   int level = 0;
-  uint32_t rp4 = static_cast<uint32_t>(4 * (a_begin - a0));
   const uint32_t sw = static_cast<uint32_t>(__cvta_generic_to_shared(words));
+  uint32_t rp = sw + static_cast<uint32_t>(4 * (a_begin - a0));
+  const uint32_t cap = sw + static_cast<uint32_t>(4 * (a.stage_words - 32));
   const uint32_t sl1 = static_cast<uint32_t>(__cvta_generic_to_shared(L1));
   const uint32_t sl = static_cast<uint32_t>(__cvta_generic_to_shared(L));
   const int64_t steps = chunk / 8;
@@ -253,6 +257,9 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(const __grid_consta
   uint32_t q2 = __ldg(nib + (2 < last ? 2 : last) * 32 + lane);
   uint32_t q3 = __ldg(nib + (3 < last ? 3 : last) * 32 + lane);
   uint4 *out = reinterpret_cast<uint4 *>(out_row);
+  // Unrolled twice so that consecutive 16-byte stores take different registers:
+  // the next iteration's results need not wait for the store to read its own.
+#pragma unroll 2
   for (int64_t m = 0; m < steps; m += 2) {
     uint32_t lohi[4];
 #pragma unroll
@@ -260,18 +267,18 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(const __grid_consta
       const uint32_t nw = h ? q1 : q0;
       uint32_t acc_lo, acc_hi;
       {
-        uint32_t ent = step_staged(buf, level, rp4, sw, sl1, sl, lt);
+        uint32_t ent = step_staged(buf, level, rp, cap, sl1, sl, lt);
         acc_lo = ent >> 1;
 #pragma unroll
         for (int k = 1; k < 4; ++k) {
-          ent = step_staged(buf, level, rp4, sw, sl1, sl, lt);
+          ent = step_staged(buf, level, rp, cap, sl1, sl, lt);
           acc_lo += ent << (8 * k - 1);
         }
-        ent = step_staged(buf, level, rp4, sw, sl1, sl, lt);
+        ent = step_staged(buf, level, rp, cap, sl1, sl, lt);
         acc_hi = ent >> 1;
 #pragma unroll
         for (int k = 1; k < 4; ++k) {
-          ent = step_staged(buf, level, rp4, sw, sl1, sl, lt);
+          ent = step_staged(buf, level, rp, cap, sl1, sl, lt);
           acc_hi += ent << (8 * k - 1);
         }
       }
@@ -284,6 +291,19 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(const __grid_consta
     q2 = __ldg(nib + (m + 4 < last ? m + 4 : last) * 32 + lane);
     q3 = __ldg(nib + (m + 5 < last ? m + 5 : last) * 32 + lane);
   }
+}
+
+// Words per warp buffer for records of pitch P holding N values: the mean
+// Huffman words per group when the record is full, plus an eighth for groups
+// above the mean and the 32 words of refill slack; groups larger than that take
+// the register-window path.  A smaller buffer fits more CTAs per SM.
+int64_t stage_words_for(int64_t P, int64_t N, int64_t chunk) {
+  const int64_t G = N / (32 * chunk);
+  const int64_t huff = (P - 4 * (G + 1) - N / 2) / 4;
+  const int64_t mean = (huff + G - 1) / G;
+  int64_t w = mean + mean / 8 + 32;
+  w = (w + 3) / 4 * 4;
+  return w < kStageMin ? kStageMin : (w > kStageMax ? kStageMax : w);
 }
 
 }  // namespace
@@ -321,8 +341,16 @@ extern "C" int xp_decode_rows(const int64_t *todo, int64_t K, const int64_t *dst
     a.n[i] = DName{static_cast<const uint8_t *>(stgs[i]), P, static_cast<uint8_t *>(dsts[i]), N,
                    N / (32 * chunk)};
   }
+  const int64_t sw0 = stage_words_for(P0, N0, chunk), sw1 = stage_words_for(P1, N1, chunk);
+  a.stage_words = sw0 > sw1 ? sw0 : sw1;
+  const size_t smem = static_cast<size_t>(kWarps * 4 * a.stage_words);
+  if (smem > 48 * 1024) {
+    cudaError_t err = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(smem));
+    if (err != cudaSuccess) return static_cast<int>(err);
+  }
   const int64_t groups = a.n[0].G + a.n[1].G;
   dim3 grid(static_cast<unsigned>((groups + kWarps - 1) / kWarps), static_cast<unsigned>(K));
-  decode_kernel<<<grid, kWarps * 32, 0, as_stream(stream)>>>(a);
+  decode_kernel<<<grid, kWarps * 32, smem, as_stream(stream)>>>(a);
   return launch_status();
 }

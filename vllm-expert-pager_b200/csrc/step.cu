@@ -93,13 +93,11 @@ __global__ void __launch_bounds__(gdev::kThreads) step_kernel(const __grid_const
   if (role < 2) {
     const int64_t S = p.a.slots > p.b.slots ? p.a.slots : p.b.slots;
     TableSmem sm = tdev::carve(smem, p.E, S);
-    if (role == 0) {
-      tdev::need_and_table(sm, p.a, p.ids, p.ids_bytes, p.K, p.E);
-      tdev::acquire_table(sm, p.a, p.E, p.K, p.map32, nullptr, p.a_slot, p.a_todo, true, true);
-    } else {
-      tdev::need_and_table(sm, p.b, p.ids, p.ids_bytes, p.K, p.E);
-      tdev::acquire_table(sm, p.b, p.E, p.K, nullptr, nullptr, p.b_slot, p.b_todo, true, true);
-    }
+    const bool vram = role == 0;
+    const tdev::Table t = vram ? p.a : p.b;
+    tdev::need_and_table(sm, t, p.ids, p.ids_bytes, p.K, p.E);
+    tdev::acquire_table(sm, t, p.E, p.K, vram ? p.map32 : nullptr, nullptr,
+                        vram ? p.a_slot : p.b_slot, vram ? p.a_todo : p.b_todo, true, true);
     raise_flag(&flags[0]);
   } else if (p.fetch && role == static_cast<int>(gridDim.x) - 1) {
     if (wait_flag(&flags[0], 2, p.table_wait_ns, &flags[3])) {

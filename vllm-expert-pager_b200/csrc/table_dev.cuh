@@ -16,7 +16,7 @@ constexpr int kThreads = 256;
 // (table.py:14-16).
 constexpr unsigned long long kProtect = 1ull << 40;
 
-using BlockScan = cub::BlockScan<int, kThreads>;
+using BlockScan = cub::BlockScan<int, kThreads, cub::BLOCK_SCAN_WARP_SCANS>;
 
 // Shared memory of one table update.  Each table is read from global memory
 // once, with coalesced loads, into slot/occ/key; the update then works on
@@ -64,15 +64,28 @@ struct Table {
   int64_t slots;
 };
 
-// Copy of the table into shared memory (no barrier).
+// Copy of the table into shared memory (no barrier).  Each thread's first
+// elements are loaded into registers before any shared store, so that their
+// global loads are in flight together (the shared arrays are reached through
+// generic pointers, which the compiler cannot tell apart from global ones).
 __device__ inline void load_table(const TableSmem &sm, Table t, int64_t E) {
   const int tid = threadIdx.x;
-  if (tid == 0) *sm.step = t.counters[0];
-  for (int64_t s = tid; s < t.slots; s += kThreads) {
+  const int64_t S = t.slots;
+  const int64_t occ0 = tid < S ? t.expert_in[tid] : 0;
+  const int64_t key0 = tid < S ? t.last_used[tid] : 0;
+  const int64_t slot0 = tid < E ? t.slot_of[tid] : 0;
+  const int64_t step0 = tid == 0 ? t.counters[0] : 0;
+  if (tid == 0) *sm.step = step0;
+  if (tid < S) {
+    sm.occ[tid] = static_cast<int>(occ0);
+    sm.key[tid] = static_cast<unsigned long long>(key0);
+  }
+  if (tid < E) sm.slot[tid] = static_cast<int>(slot0);
+  for (int64_t s = tid + kThreads; s < S; s += kThreads) {
     sm.occ[s] = static_cast<int>(t.expert_in[s]);
     sm.key[s] = static_cast<unsigned long long>(t.last_used[s]);
   }
-  for (int64_t e = tid; e < E; e += kThreads) sm.slot[e] = static_cast<int>(t.slot_of[e]);
+  for (int64_t e = tid + kThreads; e < E; e += kThreads) sm.slot[e] = static_cast<int>(t.slot_of[e]);
 }
 
 // need[e] = e occurs in ids[0:K] (table.py:63-71) and the table copy, with the
