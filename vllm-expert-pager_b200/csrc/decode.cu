@@ -18,9 +18,11 @@
 //    a refill is one conflict-free shared load.  A group larger than the
 //    per-warp buffer (flat exponent histograms only) takes a slower path that
 //    streams the words through a register window.
-//  * LUT lookups go to a 128-byte first-level table: its 32 words sit in 32
-//    distinct banks, so a warp's lookups never conflict.  Codes longer than 7
-//    bits (rare) fall back to the full 512-byte table.
+//  * One unconditional lookup in the 512-byte LUT per symbol (the table is
+//    512-byte aligned, so its address is one AND/OR of the window).  A two-level
+//    lookup (a conflict-free 128-byte table for codes up to 7 bits, then a
+//    predicated load of the full table) measured 12 % slower: the predicated
+//    load stays on the symbol-to-symbol chain even when no lane takes it.
 //  * Exponent bits of 4 symbols are summed into one word with one multiply-add
 //    each (the bit fields do not overlap) and masked once; sign/mantissa
 //    nibbles are spread to bytes with six bit operations per 4 values.
@@ -79,20 +81,20 @@ __device__ __forceinline__ uint32_t spread(uint32_t x) {
 // One symbol step for lane state (buf, level): refill (warp-collective), look
 // up, consume; returns the LUT entry.  Written in PTX, without branches.
 // Shared-memory addresses are 32-bit: rp (the next unread word of the staged
-// stream), lut1 (128 B) and lut (512 B).  The refilling lanes' word is the
+// stream) and lut (512 B, 512-aligned).  The refilling lanes' word is the
 // popc(bal & lt)-th after rp; rp is clamped to cap after each advance, off the
 // symbol-to-symbol chain, so that rp + 4 * 31 stays inside the warp's buffer
 // (a refilling lane of a valid record never leaves its group's words, which
 // end at least 32 words before the buffer's end); buf |= w << level is one wide
-// multiply-add because the new bits lie above level; the 512-byte LUT is read
-// only by lanes whose code is longer than 7 bits (predicated load).
+// multiply-add because the new bits lie above level; the LUT address is the
+// table's base OR the low 9 bits of the buffer.
 __device__ __forceinline__ uint32_t step_staged(uint64_t &buf, int &level, uint32_t &rp,
-                                                uint32_t cap, uint32_t lut1, uint32_t lut,
+                                                uint32_t cap, uint32_t lut,
                                                 unsigned lt) {
   uint32_t ent;
   asm volatile(
       "{\n\t"
-      ".reg .pred p, q;\n\t"
+      ".reg .pred p;\n\t"
       ".reg .b32 bal, t, c, a, w, m, n, x, len;\n\t"
       "setp.lt.s32 p, %1, 9;\n\t"
       "vote.sync.ballot.b32 bal, p, 0xffffffff;\n\t"
@@ -108,19 +110,15 @@ __device__ __forceinline__ uint32_t step_staged(uint64_t &buf, int &level, uint3
       "mad.lo.u32 %2, n, 4, %2;\n\t"
       "min.u32 %2, %2, %5;\n\t"
       "cvt.u32.u64 x, %0;\n\t"
-      "and.b32 t, x, 127;\n\t"
-      "add.u32 t, t, %6;\n\t"
-      "ld.shared.u8 %3, [t];\n\t"
-      "setp.eq.u32 q, %3, 0;\n\t"
       "and.b32 t, x, 511;\n\t"
-      "add.u32 t, t, %7;\n\t"
-      "@q ld.shared.u8 %3, [t];\n\t"
+      "or.b32 t, t, %6;\n\t"
+      "ld.shared.u8 %3, [t];\n\t"
       "and.b32 len, %3, 15;\n\t"
       "shr.b64 %0, %0, len;\n\t"
       "sub.s32 %1, %1, len;\n\t"
       "}"
       : "+l"(buf), "+r"(level), "+r"(rp), "=r"(ent)
-      : "r"(lt), "r"(cap), "r"(lut1), "r"(lut));
+      : "r"(lt), "r"(cap), "r"(lut));
   return ent;
 }
 
@@ -128,7 +126,7 @@ __device__ __forceinline__ uint32_t step_staged(uint64_t &buf, int &level, uint3
 // register window slid with coalesced loads, words handed out by shuffles.
 __device__ void decode_group_window(const uint32_t *huff, int64_t wbase, int64_t rend,
                                     const uint32_t *nib, uint8_t *out_row, int64_t chunk,
-                                    const uint8_t *L1, const uint8_t *L, int lane) {
+                                    const uint8_t *L, int lane) {
   auto ld = [&](int64_t idx) -> uint32_t {
     return (idx >= 0 && idx < rend) ? __ldg(huff + idx) : 0u;
   };
@@ -161,8 +159,7 @@ __device__ void decode_group_window(const uint32_t *huff, int64_t wbase, int64_t
           w2 = ld(wbase + 64 + lane);
         }
       }
-      uint32_t ent = L1[buf & 127];
-      if ((ent & 15) == 0) ent = L[buf & (kLutBytes - 1)];
+      const uint32_t ent = L[buf & (kLutBytes - 1)];
       const uint32_t len = ent & 15;
       buf >>= len;
       level -= static_cast<int>(len);
@@ -177,48 +174,53 @@ __device__ void decode_group_window(const uint32_t *huff, int64_t wbase, int64_t
 
 __global__ void __launch_bounds__(kWarps * 32) decode_kernel(const __grid_constant__ DecodeArgs a) {
   extern __shared__ __align__(16) uint32_t s_words[];  // [kWarps][stage_words]
-  __shared__ __align__(16) uint8_t s_lut[kWarps][kLutBytes];
-  __shared__ __align__(16) uint8_t s_lut1[kWarps][128];
-  const int64_t j = blockIdx.y;
-  const int64_t e = a.todo[j];
-  if (e < 0) return;
-  if (a.skip)
-    for (int64_t k = 0; k < a.K; ++k)
-      if (a.skip[k] == e) return;
-  if (a.cache_row[e] >= 0) return;  // copied raw from the cache slab
+  __shared__ __align__(512) uint8_t s_lut[kWarps][kLutBytes];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t j = blockIdx.y;
   const int64_t gg = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
   if (gg >= a.n[0].G + a.n[1].G) return;
   const int which = gg < a.n[0].G ? 0 : 1;
   const DName &n = a.n[which];
   const int64_t g = which ? gg - a.n[0].G : gg;
-  int64_t dst_row = a.dst_row[e];
-  dst_row = dst_row > 0 ? dst_row : 0;
   const int64_t chunk = a.chunk, G = n.G;
   const uint8_t *rec = n.stg + j * n.P;
   const int64_t head = 4 * (G + 1);
   const int32_t *hdr = reinterpret_cast<const int32_t *>(rec);
   const int64_t huff_w = (head + n.N / 2) / 4;  // first Huffman word, from the record start
   const int64_t rec_w = n.P / 4;
-  // Words of this group: [gstart[g], gstart[g+1]), never past the record.
+  // The prologue takes three round trips to global memory.  First: the todo
+  // entry and the group's word range [gstart[g], gstart[g+1]) from the header of
+  // staging row j (row j exists for every todo index).
+  const int64_t e = a.todo[j];
   int64_t w_begin = hdr[g], w_end = hdr[g + 1];
-  if (w_end > rec_w - huff_w) w_end = rec_w - huff_w;
-  if (w_begin > w_end) w_begin = w_end;
-
+  if (e < 0) return;
+  // Second, in flight together: the skip list (one entry per lane), the
+  // expert's cache and destination rows and its LUT.
+  const int64_t sk0 = (a.skip && lane < a.K) ? a.skip[lane] : -1;
+  const int64_t crow = a.cache_row[e];
+  int64_t dst_row = a.dst_row[e];
+  const uint4 lut_v = reinterpret_cast<const uint4 *>(a.lut + (e * 2 + which) * kLutBytes)[lane];
+  bool skipped = __any_sync(kFull, sk0 == e);
+  if (a.skip)
+    for (int64_t k0 = 32; k0 < a.K; k0 += 32) {
+      const int64_t k = k0 + lane;
+      skipped |= __any_sync(kFull, k < a.K && a.skip[k] == e);
+    }
+  // Skipped, or copied raw from the cache slab: the staging row holds no record
+  // of this expert, and nothing past its header is read.
+  if (skipped || crow >= 0) return;
+  // Third: the group's words, clamped to the record (a corrupt header cannot
+  // move a read outside row j).
+  const int64_t wmax = rec_w - huff_w;
+  w_end = w_end < 0 ? 0 : (w_end > wmax ? wmax : w_end);
+  w_begin = w_begin < 0 ? 0 : (w_begin > w_end ? w_end : w_begin);
   uint8_t *L = s_lut[warp];
-  uint8_t *L1 = s_lut1[warp];
-  reinterpret_cast<uint4 *>(L)[lane] =
-      reinterpret_cast<const uint4 *>(a.lut + (e * 2 + which) * kLutBytes)[lane];
-  __syncwarp();
-  for (int i = lane; i < 128; i += 32) {
-    uint8_t v = L[i];
-    L1[i] = (v & 15) <= 7 ? v : 0;
-  }
+  reinterpret_cast<uint4 *>(L)[lane] = lut_v;
+  dst_row = dst_row > 0 ? dst_row : 0;
   const uint32_t *nib = reinterpret_cast<const uint32_t *>(rec + head) + g * (chunk / 8) * 32;
   uint8_t *out_row = n.dst + dst_row * n.N + (g * 32 + lane) * chunk;
-
-  // Copy the group's words into shared memory in 16-byte units aligned to the
-  // record (4096-aligned rows, so record word 4u is 16-byte aligned).
+  // The words go to shared memory in 16-byte units aligned to the record
+  // (4096-aligned rows, so record word 4u is 16-byte aligned).
   const int64_t a_begin = huff_w + w_begin, a_end = huff_w + w_end;
   const int64_t a0 = a_begin & ~int64_t(3);
   const int64_t units = (a_end - a0 + 3) / 4;
@@ -226,7 +228,7 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(const __grid_consta
   if (!staged) {
     __syncwarp();
     decode_group_window(reinterpret_cast<const uint32_t *>(rec) + huff_w, w_begin,
-                        w_end, nib, out_row, chunk, L1, L, lane);
+                        w_end, nib, out_row, chunk, L, lane);
     return;
   }
   uint32_t *words = s_words + warp * a.stage_words;
@@ -245,7 +247,6 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(const __grid_consta
   const uint32_t sw = static_cast<uint32_t>(__cvta_generic_to_shared(words));
   uint32_t rp = sw + static_cast<uint32_t>(4 * (a_begin - a0));
   const uint32_t cap = sw + static_cast<uint32_t>(4 * (a.stage_words - 32));
-  const uint32_t sl1 = static_cast<uint32_t>(__cvta_generic_to_shared(L1));
   const uint32_t sl = static_cast<uint32_t>(__cvta_generic_to_shared(L));
   const int64_t steps = chunk / 8;
   // Nibble words are prefetched two iterations ahead.  The index is clamped
@@ -267,18 +268,18 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(const __grid_consta
       const uint32_t nw = h ? q1 : q0;
       uint32_t acc_lo, acc_hi;
       {
-        uint32_t ent = step_staged(buf, level, rp, cap, sl1, sl, lt);
+        uint32_t ent = step_staged(buf, level, rp, cap, sl, lt);
         acc_lo = ent >> 1;
 #pragma unroll
         for (int k = 1; k < 4; ++k) {
-          ent = step_staged(buf, level, rp, cap, sl1, sl, lt);
+          ent = step_staged(buf, level, rp, cap, sl, lt);
           acc_lo += ent << (8 * k - 1);
         }
-        ent = step_staged(buf, level, rp, cap, sl1, sl, lt);
+        ent = step_staged(buf, level, rp, cap, sl, lt);
         acc_hi = ent >> 1;
 #pragma unroll
         for (int k = 1; k < 4; ++k) {
-          ent = step_staged(buf, level, rp, cap, sl1, sl, lt);
+          ent = step_staged(buf, level, rp, cap, sl, lt);
           acc_hi += ent << (8 * k - 1);
         }
       }
