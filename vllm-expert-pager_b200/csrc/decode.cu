@@ -26,8 +26,8 @@
 //  * Exponent bits of 4 symbols are summed into one word with one multiply-add
 //    each (the bit fields do not overlap) and masked once; sign/mantissa
 //    nibbles are spread to bytes with six bit operations per 4 values.
-//  * Each lane stores 16 bytes per 16 symbols; nibble words are prefetched
-//    four steps ahead.
+//  * Each lane stores 16 bytes per 16 symbols; nibble words are loaded two
+//    iterations ahead and prefetched into L2 eight iterations ahead.
 #include "common.cuh"
 
 namespace xp {
@@ -249,10 +249,15 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(const __grid_consta
   const uint32_t cap = sw + static_cast<uint32_t>(4 * (a.stage_words - 32));
   const uint32_t sl = static_cast<uint32_t>(__cvta_generic_to_shared(L));
   const int64_t steps = chunk / 8;
-  // Nibble words are prefetched two iterations ahead.  The index is clamped
-  // (steps is even and at least 2) rather than the load predicated, so that no
-  // select consumes a load right after it is issued.
+  // Nibble words are loaded into registers two iterations ahead, and their
+  // 128-byte lines are prefetched into L2 sixteen words (eight iterations) ahead,
+  // which hides the HBM latency that the register prefetch alone leaves exposed
+  // (7 % of the kernel at 8 rows per launch).  The index is clamped (steps is even
+  // and at least 2) rather than the load predicated, so that no select consumes
+  // a load right after it is issued.
   const int64_t last = steps - 1;
+  for (int64_t i = lane; i < 16 && i <= last; i += 32)
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(nib + i * 32));
   uint32_t q0 = __ldg(nib + lane);
   uint32_t q1 = __ldg(nib + 32 + lane);
   uint32_t q2 = __ldg(nib + (2 < last ? 2 : last) * 32 + lane);
@@ -289,6 +294,8 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(const __grid_consta
     out[m / 2] = make_uint4(lohi[0], lohi[1], lohi[2], lohi[3]);
     q0 = q2;
     q1 = q3;
+    if (lane < 2 && m + 16 + lane <= last)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(nib + (m + 16 + lane) * 32));
     q2 = __ldg(nib + (m + 4 < last ? m + 4 : last) * 32 + lane);
     q3 = __ldg(nib + (m + 5 < last ? m + 5 : last) * 32 + lane);
   }
