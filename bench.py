@@ -607,6 +607,35 @@ def run_model_workload(args):
         dist.destroy_process_group()
 
 
+def bench_encode(device, copies: int = 8, reps: int = 3) -> dict:
+    """GPU encoder (xp_encode_rows) on config-1 rows: the 8 experts' rows of each name,
+    repeated ``copies`` times, one batched call per name; raw bytes / wall time of the
+    two calls (each reads the record sizes back to check the pitch), best of ``reps``."""
+    from vllm_expert_pager import codec, synthetic
+
+    experts = synthetic.fp8_experts(8, seed=0)
+    batches = []
+    for name in synthetic.SHAPES:
+        rows = torch.stack([synthetic.row_bytes(ex[name][0]) for ex in experts] * copies)
+        batches.append((rows.to(device), codec.pitch_of(rows.shape[1], 0.89, 4096)))
+    raw = sum(b.numel() for b, _ in batches)
+    for b, p in batches:  # warm-up
+        codec.encode_rows(b, p)
+    torch.cuda.synchronize()
+    best = None
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        for b, p in batches:
+            codec.encode_rows(b, p)
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        best = dt if best is None else min(best, dt)
+    return {"value": round(raw / best / 1e9, 2), "unit": "GB/s", "raw_bytes": raw,
+            "rows": sum(b.shape[0] for b, _ in batches),
+            "how": "encode_rows of 8 x config-1 experts per name, repeated "
+                   f"{copies}x, raw bytes / wall time incl. the pitch check, best of {reps}"}
+
+
 def bench_acquire(device, steps: int = 1024) -> dict:
     """Both LRU table updates of a decode step (xp_acquire_pair) on the config-2 trace:
     device time per launch, and the reference algorithm's port on one host core."""
@@ -1033,6 +1062,7 @@ def main():
         for k in (8, 64):
             print(json.dumps({"decode": bench_decode(device, k)}), flush=True)
         print(json.dumps({"acquire_pair": bench_acquire(device)}), flush=True)
+        print(json.dumps({"encode_gpu": bench_encode(device)}), flush=True)
         from vllm_expert_pager import synthetic
         from vllm_expert_pager.table import ExpertTable
 
@@ -1108,7 +1138,7 @@ def main():
     achieved = moved / (gather_ms * 1e-3) / 1e9 if gather_ms > 0 else None
 
     kernels = {"decode_k8": bench_decode(device, 8), "decode_k64": bench_decode(device, 64),
-               "acquire_pair": bench_acquire(device)}
+               "acquire_pair": bench_acquire(device), "encode_gpu": bench_encode(device)}
 
     cpu = None
     if rank == 0 and world == 1:

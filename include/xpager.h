@@ -221,6 +221,20 @@ int xp_decode_rows(const int64_t *todo, int64_t K, const int64_t *dst_row,
                    const void *stg1, int64_t P1, void *dst1, int64_t N1,
                    const int64_t *skip, int64_t chunk, void *stream);
 
+/* Replaces codec.encode (codec.py:125-193), which the reference runs as torch
+ * ops on the GPU while loading weights (store.py:576-599), for a batch of rows:
+ * raw[rows][n] (device, 16-byte aligned) -> records[rows][pitch] (zero padded
+ * past each record's used bytes) and luts[rows][512], byte-identical to the
+ * reference.  used[rows] (device) receives each record's used bytes; a row with
+ * used > pitch is not written (the caller checks, as codec.py:157-162 raises).
+ * scratch: device memory of at least xp_encode_scratch_bytes(rows, n, chunk)
+ * bytes, 256-byte aligned.  n must be a multiple of 32*chunk, chunk of 8; rows
+ * <= 65535.  Five launches on `stream`, no allocation, no synchronisation. */
+int64_t xp_encode_scratch_bytes(int64_t rows, int64_t n, int64_t chunk);
+int xp_encode_rows(const void *raw, int64_t rows, int64_t n, int64_t pitch, int64_t chunk,
+                   void *records, void *luts, int64_t *used, void *scratch,
+                   int64_t scratch_bytes, void *stream);
+
 /* ---- host side ---- */
 
 /* Replaces codec.encode (codec.py:125-193) on the host: compress raw[n] into

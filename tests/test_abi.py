@@ -49,3 +49,17 @@ def test_device_calls_reject_bad_arguments_before_launching():
     assert lib.xp_decode_rows(None, 1, None, None, None, None, 0, None, 0, None, 0, None, 0,
                               None, 7, None) == native.XP_EINVAL
     assert lib.xp_fetch_wait(None, 1, None, None, None, 256, 4, 1, 1, None) == native.XP_EINVAL
+
+
+def test_encode_scratch_size_and_argument_checks():
+    lib = native.lib()
+    # 2 MiB rows, chunk 512: G = 128 groups -> 256-byte-rounded per-row scratch.
+    per_row = lib.xp_encode_scratch_bytes(1, 2 * 1024 * 1024, 512)
+    assert per_row > 0 and per_row % 256 == 0 and per_row >= 4 * (2 * 128 + 1)
+    assert lib.xp_encode_scratch_bytes(8, 2 * 1024 * 1024, 512) == 8 * per_row
+    assert lib.xp_encode_scratch_bytes(1, 1000, 512) == -1  # not a multiple of 32 * chunk
+    assert lib.xp_encode_scratch_bytes(1, 4096, 12) == -1   # chunk not a multiple of 8
+    assert lib.xp_encode_rows(None, 1, 4096, 8192, 64, None, None, None, None, 0,
+                              None) == native.XP_EINVAL
+    assert lib.xp_encode_rows(None, 0, 4096, 8192, 64, None, None, None, None, 0,
+                              None) == native.XP_OK

@@ -7,9 +7,10 @@ lane) order, then the Huffman words of each group in refill order.  Exponent
 codes are canonical, bit-reversed and at most LIMIT bits; the 512-byte LUT of a
 row lives in a VRAM table, not in the record.
 
-``encode`` runs at load time in the native library (encode.cpp, a loop over the
-row on the host); ``decode_rows`` expands staging rows on the GPU
-(decode.cu).
+``encode`` runs at load time: rows on a GPU are encoded there in batches
+(``encode_rows``, encode_gpu.cu), as the reference encodes with torch ops on the
+GPU; rows on the host go to the native host encoder (encode.cpp).
+``decode_rows`` expands staging rows on the GPU (decode.cu).
 """
 
 from __future__ import annotations
@@ -41,14 +42,70 @@ def groups(n_bytes: int, chunk: int = CHUNK) -> int:
     return n_bytes // (chunk * LANES)
 
 
+def _pitch_error(nbytes: int, pitch: int, N: int) -> ValueError:
+    return ValueError(
+        f"compressed row is {nbytes} B, pitch is {pitch} B; "
+        f"VLLM_EXPERT_PAGER_PITCH must be at least {nbytes / N:.4f}"
+    )
+
+
+# Rows per launch of the GPU encoder (its grid's y extent).
+_ENCODE_BATCH = 65535
+
+
+def encode_rows(raw: torch.Tensor, pitch: int, chunk: int = CHUNK) -> tuple[torch.Tensor, torch.Tensor]:
+    """Compress uint8 rows ``(R, N)`` on their GPU (encode_gpu.cu).
+
+    Returns ``(records (R, pitch), LUTs (R, 512))`` on raw's device, each row
+    byte-identical to codec.encode of the reference (codec.py:125-193).  Raises
+    ValueError, as the reference does for its row, if a row does not fit in the
+    record; this reads the record sizes back (one synchronisation per call).
+    """
+    native.require_cuda(raw)
+    raw = raw.detach().contiguous().view(torch.uint8)
+    raw = raw.reshape(raw.shape[0], -1) if raw.dim() > 1 else raw.reshape(1, -1)
+    if raw.data_ptr() % 16:
+        raw = raw.clone()
+    R, N = raw.shape
+    if N % (chunk * LANES):
+        raise ValueError(f"row of {N} values is not a multiple of {chunk * LANES}")
+    dev = raw.device
+    records = torch.empty((R, pitch), dtype=torch.uint8, device=dev)
+    luts = torch.empty((R, LUT_BYTES), dtype=torch.uint8, device=dev)
+    used = torch.empty((R,), dtype=torch.int64, device=dev)
+    lib = native.lib()
+    for r0 in range(0, R, _ENCODE_BATCH):
+        r1 = min(R, r0 + _ENCODE_BATCH)
+        nb = lib.xp_encode_scratch_bytes(r1 - r0, N, chunk)
+        if nb < 0:
+            raise ValueError(f"cannot encode rows of {N} values with chunk {chunk}")
+        scratch = torch.empty((max(nb, 1),), dtype=torch.uint8, device=dev)
+        native.check(
+            lib.xp_encode_rows(raw[r0].data_ptr(), r1 - r0, N, pitch, chunk,
+                               records[r0].data_ptr(), luts[r0].data_ptr(),
+                               used[r0:].data_ptr(), scratch.data_ptr(), nb,
+                               native.stream_of(dev)),
+            "encode_rows",
+        )
+    over = (used > pitch).nonzero()
+    if over.numel():
+        raise _pitch_error(int(used[int(over[0])]), pitch, N)
+    return records, luts
+
+
 def encode(raw: torch.Tensor, pitch: int, chunk: int = CHUNK) -> tuple[torch.Tensor, torch.Tensor]:
     """Compress a uint8 row (N,). Returns ``(record of pitch bytes, 512 B LUT)`` on raw's device.
 
-    Raises ValueError if the row does not fit in the record (codec.py:125-193).
+    A row on a GPU is encoded there (``encode_rows``); a row on the host by the
+    native host encoder.  Raises ValueError if the row does not fit in the
+    record (codec.py:125-193).
     """
     N = raw.numel()
     if N % (chunk * LANES):
         raise ValueError(f"row of {N} values is not a multiple of {chunk * LANES}")
+    if raw.is_cuda:
+        records, luts = encode_rows(raw.reshape(1, -1), pitch, chunk)
+        return records[0], luts[0]
     host = np.ascontiguousarray(raw.reshape(-1).detach().cpu().numpy().view(np.uint8))
     record = np.empty(pitch, dtype=np.uint8)
     lut = np.empty(LUT_BYTES, dtype=np.uint8)
@@ -56,11 +113,7 @@ def encode(raw: torch.Tensor, pitch: int, chunk: int = CHUNK) -> tuple[torch.Ten
     rc = native.lib().xp_encode_row(host.ctypes.data, N, pitch, chunk, record.ctypes.data,
                                     lut.ctypes.data, ctypes.byref(used))
     if rc == native.XP_EPITCH:
-        nbytes = used.value
-        raise ValueError(
-            f"compressed row is {nbytes} B, pitch is {pitch} B; "
-            f"VLLM_EXPERT_PAGER_PITCH must be at least {nbytes / N:.4f}"
-        )
+        raise _pitch_error(used.value, pitch, N)
     native.check(rc, "encode")
     return (torch.from_numpy(record).to(raw.device), torch.from_numpy(lut).to(raw.device))
 

@@ -62,6 +62,8 @@ _SIGNATURES = {
     "xp_decode_rows": (_i32, [_p, _i64, _p, _p, _p, _p, _i64, _p, _i64, _p, _i64, _p, _i64, _p,
                               _i64, _p]),
     "xp_encode_row": (_i32, [_p, _i64, _i64, _i64, _p, _p, ctypes.POINTER(_i64)]),
+    "xp_encode_scratch_bytes": (_i64, [_i64, _i64, _i64]),
+    "xp_encode_rows": (_i32, [_p, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _p]),
     "xp_pinned_alloc": (_i32, [_i64, _i32, ctypes.POINTER(_p), ctypes.POINTER(_p)]),
     "xp_pinned_free": (_i32, [_p, _i64]),
     "xp_device_pointer": (_i32, [_p, ctypes.POINTER(_p)]),

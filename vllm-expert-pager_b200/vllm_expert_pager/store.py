@@ -312,13 +312,16 @@ class Store:
                 f"expected {self.row_bytes[name]}"
             )
         if self.compress:
-            record, lut = codec.encode(raw.cpu(), self.pitch[name])
+            # Encoded on the GPU when the store has one (encode_gpu.cu), as the
+            # reference encodes with torch ops on the device (store.py:588).
+            src = raw.to(self.device) if self.device.type == "cuda" else raw.cpu()
+            record, lut = codec.encode(src, self.pitch[name])
             self.lut[layer, expert, self.names.index(name)] = lut.to(self.device)
             words = record.view(torch.int32)
         else:
-            words = raw.cpu().view(torch.int32)
+            words = raw.view(torch.int32)
         if expert < self.ram_slots:
             self.pinned[name][layer * self.ram_slots + expert].copy_(words)
         if self.fd_w is not None:
             offset = (layer * self.num_experts + expert) * self.record_bytes + self.offset[name]
-            os.pwrite(self.fd_w, memoryview(np.ascontiguousarray(words.numpy())), offset)
+            os.pwrite(self.fd_w, memoryview(np.ascontiguousarray(words.cpu().numpy())), offset)
