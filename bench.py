@@ -802,6 +802,28 @@ def time_planning(table_cls, syn, device, layers: int = 40, reps: int = 3) -> di
             "how": f"{layers} layers back to back, eager, best of {reps}"}
 
 
+def time_planning_fused(device, layers: int = 40, reps: int = 3) -> dict:
+    """The same planning as ``time_planning`` through this library's one-launch
+    ``WorkingPlan`` (xp_plan_working), which ``LayerPager`` uses."""
+    from vllm_expert_pager import synthetic as syn
+    from vllm_expert_pager.table import ExpertTable, WorkingPlan
+
+    e_, s_, r_, w_ = 256, 32, 128, 64
+    ids = syn.uniform_routing(2048, e_, 8, seed=0).to(device)
+    vram, ram = ExpertTable(e_, s_, device), ExpertTable(e_, r_, device)
+    warm = syn.zipf_trace(64, e_, 8, 1.1, layer=0).to(device)
+    for i in range(64):
+        vram.acquire(warm[i])
+    planner = WorkingPlan(e_, w_, r_, s_, device)
+    for _ in range(3):
+        planner(ram, vram, ids, 0, 40 * r_)
+    torch.cuda.synchronize()
+    best = min(timed(lambda: [planner(ram, vram, ids, 0, 40 * r_) for _ in range(layers)])
+               / layers for _ in range(reps))
+    return {"ms_per_layer": round(best, 4),
+            "how": f"{layers} layers back to back, eager, one launch each, best of {reps}"}
+
+
 REF_DIR = os.path.join(ROOT, "baseline", "_ref")
 
 
@@ -1068,6 +1090,7 @@ def main():
 
         print(json.dumps({"plan_config5": time_planning(ExpertTable, synthetic, device)}),
               flush=True)
+        print(json.dumps({"plan_config5_fused": time_planning_fused(device)}), flush=True)
         return
     if args.ctas:
         gather_mod.GATHER_CTAS = args.ctas

@@ -92,6 +92,22 @@ int xp_plan_chunks(int64_t E, const int64_t *slot_of, const int64_t *before,
                    int64_t working_base, int64_t *dst_row, int64_t *src_row, int64_t *maps,
                    int64_t *todo, int64_t *ssd, int64_t *late, void *stream);
 
+/* The planning of one working-path step in one launch: replaces the sequence
+ * need_mask -> slot_of[:E].clone() -> acquire (K <= R) or seed -> plan_chunks
+ * of _expert_pager_forward_working (experts.py:500-511) on the RAM table
+ * (R slots), given the VRAM table's expert_in[S] and slot_of (cached_row[E]).
+ * Writes need[E] (uint8) and before[E] (slot_of before the update) and the
+ * outputs of xp_plan_chunks; top_in / top_out as in xp_seed.  Results equal
+ * the separate calls'.  No counterpart in the reference (it issues those
+ * steps as separate torch operations). */
+int xp_plan_working(const void *ids, int ids_bytes, int64_t K, int64_t E, int64_t *slot_of,
+                    int64_t *expert_in, int64_t *last_used, int64_t *counters, int64_t R,
+                    const int64_t *vram_expert_in, const int64_t *cached_row, int64_t S,
+                    int64_t W, int64_t ram_base, int64_t working_base, const int64_t *top_in,
+                    int64_t *top_out, uint8_t *need, int64_t *before, int64_t *dst_row,
+                    int64_t *src_row, int64_t *maps, int64_t *todo, int64_t *ssd,
+                    int64_t *late, void *stream);
+
 /* ---- gather (subsystem 2) and the SSD request ring ---- */
 
 /* Replaces gather_rows / _gather_rows_kernel (gather.py:149-194,328-393).

@@ -161,7 +161,14 @@ def test_acquire_edge_cases_match_oracle():
 PLAN_KEYS = ("dst_row", "src_row", "maps", "todo", "ssd", "late")
 
 
-def _working_step(ram, vram, ids, W, ram_base, working_base, top):
+def _working_step(ram, vram, ids, W, ram_base, working_base, top, impl="separate"):
+    """One working-step planning: the reference's separate calls, or one fused launch."""
+    if impl == "fused":
+        from vllm_expert_pager.table import WorkingPlan
+
+        plan = WorkingPlan(ram.num_experts, W, ram.num_slots, vram.num_slots, DEV)
+        need, _, out = plan(ram, vram, ids, ram_base, working_base, top)
+        return need, out
     E = ram.num_experts
     need = ram.need_mask(ids)
     cached_row = vram.slot_of[:E].clone()
@@ -173,11 +180,12 @@ def _working_step(ram, vram, ids, W, ram_base, working_base, top):
     return need, ram.plan_chunks(before, need, cached_row, W, ram_base, working_base)
 
 
+@pytest.mark.parametrize("impl", ["separate", "fused"])
 @pytest.mark.parametrize(
     "case", ["prefill_r128", "prefill_r256", "batch8_r128", "sc_seed", "sc_acquire",
              "sc_alternate", "sc_negative"]
 )
-def test_working_cases_match_reference(case):
+def test_working_cases_match_reference(case, impl):
     from vllm_expert_pager.table import ExpertTable
 
     g = load("working.npz")
@@ -188,7 +196,7 @@ def test_working_cases_match_reference(case):
     top = g[f"{case}_top"]
     ids = torch.from_numpy(g[f"{case}_ids"].astype(np.int64)).to(DEV)
     need, plan = _working_step(ram, vram, ids, W, layer * R, L * R,
-                               torch.from_numpy(top).to(DEV) if top.size else None)
+                               torch.from_numpy(top).to(DEV) if top.size else None, impl)
     for key, got in zip(PLAN_KEYS, plan):
         assert np.array_equal(got.cpu().numpy(), g[f"{case}_{key}"]), key
     for key in ("slot_of", "expert_in", "last_used"):
@@ -197,8 +205,9 @@ def test_working_cases_match_reference(case):
     assert ram.counters.cpu().tolist() == g[f"{case}_post_ram_counters"].tolist()
 
 
+@pytest.mark.parametrize("impl", ["separate", "fused"])
 @pytest.mark.parametrize("case", ["prefill_r128", "prefill_r256"])
-def test_seed_tie_rule_matches_oracle(case):
+def test_seed_tie_rule_matches_oracle(case, impl):
     """Without a replayed choice, the kernel's lowest-id tie rule equals the oracle's."""
     from oracle.table import working_step
     from vllm_expert_pager.table import ExpertTable
@@ -211,15 +220,16 @@ def test_seed_tie_rule_matches_oracle(case):
     ovram, oram = oracle_of(vram), oracle_of(ram)
     ids_np = g[f"{case}_ids"].astype(np.int64)
     _, plan = _working_step(ram, vram, torch.from_numpy(ids_np).to(DEV), W, layer * R, L * R,
-                            None)
+                            None, impl)
     _, _, _, oplan = working_step(oram, ovram, ids_np, W, layer * R, L * R)
     for key, a, b in zip(PLAN_KEYS, plan, oplan):
         assert np.array_equal(a.cpu().numpy(), b), key
     assert [digest(x) for x in oracle_of(ram).state()] == [digest(x) for x in oram.state()]
 
 
+@pytest.mark.parametrize("impl", ["separate", "fused"])
 @pytest.mark.parametrize("W", [1, 3, 4])
-def test_mixed_working_steps_match_reference(W):
+def test_mixed_working_steps_match_reference(W, impl):
     from vllm_expert_pager.table import ExpertTable
 
     g = load("working.npz")
@@ -236,7 +246,7 @@ def test_mixed_working_steps_match_reference(W):
             got = [tstate(ram), tstate(vram), digest(todo, emap, slot, vtodo)]
         else:
             top = torch.from_numpy(tops[step]).to(DEV) if len(tops[step]) else None
-            need, plan = _working_step(ram, vram, ids, W, layer * R, L * R, top)
+            need, plan = _working_step(ram, vram, ids, W, layer * R, L * R, top, impl)
             got = [tstate(ram), tstate(vram), digest(need, *plan)]
         assert got == want, f"W={W} step {step}"
 

@@ -81,9 +81,9 @@ struct SeedArgs {
   int64_t *top_out;
 };
 
-// ExpertTable.seed (table.py:140-171).
-__global__ void __launch_bounds__(kThreads) seed_kernel(const __grid_constant__ SeedArgs p) {
-  extern __shared__ __align__(16) unsigned char smem[];
+// ExpertTable.seed (table.py:140-171), run by one CTA with table_smem_bytes(E, R)
+// + 4E + 4*max(R-S,1) bytes of shared memory at smem.
+__device__ void seed_body(const SeedArgs &p, unsigned char *smem) {
   const int64_t E = p.E, R = p.t.slots, S = p.S;
   const int64_t ntop = R - S > 1 ? R - S : 1;
   TableSmem sm = carve(smem, E, R);
@@ -144,6 +144,11 @@ __global__ void __launch_bounds__(kThreads) seed_kernel(const __grid_constant__ 
   acquire_table(sm, p.t, E, S, nullptr, nullptr, nullptr, nullptr, false, false);
 }
 
+__global__ void __launch_bounds__(kThreads) seed_kernel(const __grid_constant__ SeedArgs p) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  seed_body(p, smem);
+}
+
 struct PlanArgs {
   int64_t E;
   const int64_t *slot_of, *before;
@@ -153,8 +158,8 @@ struct PlanArgs {
   int64_t *dst_row, *src_row, *maps, *todo, *ssd, *late;
 };
 
-// ExpertTable.plan_chunks (table.py:173-247).
-__global__ void __launch_bounds__(kThreads) plan_kernel(const __grid_constant__ PlanArgs p) {
+// ExpertTable.plan_chunks (table.py:173-247), run by one CTA.
+__device__ void plan_body(const PlanArgs &p) {
   __shared__ typename BlockScan::TempStorage tmp_a, tmp_b;
   const int tid = threadIdx.x;
   const int64_t E = p.E, W = p.W, N = (E + W - 1) / W + 1, NW = N * W;
@@ -206,6 +211,55 @@ __global__ void __launch_bounds__(kThreads) plan_kernel(const __grid_constant__ 
     if (ssd) p.ssd[pos] = e;
     if (need && ssd && !cached) p.late[pos] = e;
   }
+}
+
+__global__ void __launch_bounds__(kThreads) plan_kernel(const __grid_constant__ PlanArgs p) {
+  plan_body(p);
+}
+
+struct WorkArgs {
+  const void *ids;
+  int ids_bytes;
+  int64_t K, E;
+  Table t;  // the RAM table (R slots)
+  const int64_t *vram_expert_in, *cached_row;
+  int64_t S, W, ram_base, working_base;
+  const int64_t *top_in;
+  int64_t *top_out;
+  uint8_t *need;
+  int64_t *before, *dst_row, *src_row, *maps, *todo, *ssd, *late;
+};
+
+// The planning of one working-path step (experts.py:500-511) in one CTA:
+// need_mask, the copy of slot_of, acquire (K <= R) or seed, plan_chunks.
+__global__ void __launch_bounds__(kThreads) plan_working_kernel(const __grid_constant__ WorkArgs p) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int tid = threadIdx.x;
+  const int64_t E = p.E, R = p.t.slots;
+  for (int64_t e = tid; e < E; e += kThreads) {
+    p.need[e] = 0;
+    p.before[e] = p.t.slot_of[e];
+  }
+  __syncthreads();
+  for (int64_t k = tid; k < p.K; k += kThreads) {
+    const int64_t id = load_id(p.ids, p.ids_bytes, k);
+    if (id >= 0 && id < E) p.need[id] = 1;
+  }
+  __syncthreads();
+  if (p.K <= R) {  // ram.acquire(topk_ids): hits and misses are counted
+    TableSmem sm = carve(smem, E, R);
+    for (int64_t e = tid; e < E; e += kThreads) sm.need[e] = p.need[e];
+    __syncthreads();
+    acquire_table(sm, p.t, E, p.K, nullptr, nullptr, nullptr, nullptr, true, false);
+  } else {
+    const SeedArgs sa{p.ids, p.ids_bytes, p.K, E, p.t, p.vram_expert_in, p.S, p.need,
+                      p.top_in, p.top_out};
+    seed_body(sa, smem);
+  }
+  __syncthreads();
+  const PlanArgs pa{E, p.t.slot_of, p.before, p.need, p.cached_row, p.W, p.ram_base,
+                    p.working_base, p.dst_row, p.src_row, p.maps, p.todo, p.ssd, p.late};
+  plan_body(pa);
 }
 
 bool ids_ok(const void *ids, int ids_bytes, int64_t K) {
@@ -302,5 +356,28 @@ extern "C" int xp_plan_chunks(int64_t E, const int64_t *slot_of, const int64_t *
   PlanArgs p{E, slot_of, before, need, cached_row, W, ram_base, working_base,
              dst_row, src_row, maps, todo, ssd, late};
   plan_kernel<<<1, kThreads, 0, as_stream(stream)>>>(p);
+  return launch_status();
+}
+
+extern "C" int xp_plan_working(const void *ids, int ids_bytes, int64_t K, int64_t E,
+                               int64_t *slot_of, int64_t *expert_in, int64_t *last_used,
+                               int64_t *counters, int64_t R, const int64_t *vram_expert_in,
+                               const int64_t *cached_row, int64_t S, int64_t W,
+                               int64_t ram_base, int64_t working_base, const int64_t *top_in,
+                               int64_t *top_out, uint8_t *need, int64_t *before,
+                               int64_t *dst_row, int64_t *src_row, int64_t *maps, int64_t *todo,
+                               int64_t *ssd, int64_t *late, void *stream) {
+  WorkArgs p{ids, ids_bytes, K, E, Table{slot_of, expert_in, last_used, counters, R},
+             vram_expert_in, cached_row, S, W, ram_base, working_base, top_in, top_out,
+             need, before, dst_row, src_row, maps, todo, ssd, late};
+  if (!ids_ok(ids, ids_bytes, K) || !table_ok(p.t, E) || !vram_expert_in || !cached_row ||
+      !need || !before || !dst_row || !src_row || !maps || !todo || !ssd || !late)
+    return XP_EINVAL;
+  if (S < 1 || S > R || W < 1) return XP_EINVAL;
+  const int64_t ntop = R - S > 1 ? R - S : 1;
+  const size_t smem = table_smem_bytes(E, R) + 4 * E + 4 * ntop;
+  int rc = set_smem((const void *)plan_working_kernel, smem);
+  if (rc) return rc;
+  plan_working_kernel<<<1, kThreads, smem, as_stream(stream)>>>(p);
   return launch_status();
 }

@@ -33,6 +33,8 @@ _SIGNATURES = {
     "xp_seed": (_i32, [_p, _i32, _i64, _i64, _p, _p, _p, _p, _i64, _p, _i64, _p, _p, _p, _p]),
     "xp_plan_chunks": (_i32, [_i64, _p, _p, _p, _p, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p,
                               _p]),
+    "xp_plan_working": (_i32, [_p, _i32, _i64, _i64, _p, _p, _p, _p, _i64, _p, _p, _i64,
+                               _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p]),
     "xp_gather_rows": (_i32, [_p, _i64, _p, _p, _p, _i64,
                               _p, _p, _p, _p, _i64, _i64,
                               _p, _p, _p, _p, _i64, _i64,

@@ -37,7 +37,7 @@ from vllm_expert_pager.gather import (
     gather_rows,
 )
 from vllm_expert_pager.store import Store
-from vllm_expert_pager.table import ExpertTable
+from vllm_expert_pager.table import ExpertTable, WorkingPlan
 
 # Expert weights paged through the slabs, in the gather's name order.
 PARAMS = ("w13_weight", "w2_weight")
@@ -93,6 +93,7 @@ class LayerPager:
         self.ram.expert_in[:R] = self.ram.experts[:R]
         self.acquire = AcquirePair(self.vram, self.ram)
         self.expert_map = self.acquire.expert_map
+        self.planner = WorkingPlan(E, working.rows, R, S, device)
         self.scale_names = list(scales)
         self.cache_slab = {
             name: torch.empty((S, *shape), dtype=dtype, device=device)
@@ -222,18 +223,12 @@ class LayerPager:
     # ---- working path (experts.py:455-577) ----
 
     def plan(self, topk_ids: torch.Tensor):
-        """Update the RAM table and lay the step's experts out in chunks (experts.py:501-510)."""
-        store, E = self.store, self.num_experts
-        W = self.working.rows
-        need = self.ram.need_mask(topk_ids)
-        cached_row = self.vram.slot_of[:E]
-        before = self.ram.slot_of[:E].clone()
-        if topk_ids.numel() <= store.ram_slots:
-            self.ram.acquire(topk_ids)
-        else:
-            self.ram.seed(self.vram, topk_ids, need)
-        return cached_row, self.ram.plan_chunks(before, need, cached_row, W,
-                                                self.layer * store.ram_slots, store.working_base)
+        """Update the RAM table and lay the step's experts out in chunks (experts.py:501-510):
+        need_mask, the slot_of copy, acquire or seed, and plan_chunks in one launch."""
+        store = self.store
+        _, cached_row, plan = self.planner(self.ram, self.vram, topk_ids,
+                                           self.layer * store.ram_slots, store.working_base)
+        return cached_row, plan
 
     def working_chunks(self, topk_ids: torch.Tensor, run_chunk, overlap: bool = True):
         """Run the working path; ``run_chunk(k, n, slabs, expert_map)`` runs chunk k's MoE.

@@ -168,3 +168,55 @@ class ExpertTable:
             "plan_chunks",
         )
         return dst_row, src_row, maps, todo, ssd, late
+
+
+class WorkingPlan:
+    """The planning of a working-path step in one launch (xp_plan_working).
+
+    Replaces the sequence ``need_mask`` -> ``slot_of[:E].clone()`` -> ``acquire``
+    (K <= R) or ``seed`` -> ``plan_chunks`` that _expert_pager_forward_working
+    issues as separate operations (experts.py:500-511); the results are the
+    same.  The outputs live in buffers allocated here once, at fixed addresses
+    (graph-safe); each call overwrites them.
+    """
+
+    def __init__(self, num_experts: int, rows: int, ram_slots: int, vram_slots: int,
+                 device: torch.device) -> None:
+        E, W = num_experts, rows
+        self.num_experts, self.rows, self.device = E, W, torch.device(device)
+        N = -(-E // W) + 1
+        i64 = {"dtype": torch.int64, "device": self.device}
+        self.need = torch.zeros((E,), dtype=torch.uint8, device=self.device)
+        self.before = torch.empty((E,), **i64)
+        self.dst_row, self.src_row = torch.empty((E,), **i64), torch.empty((E,), **i64)
+        self.maps = torch.empty((N, E), **i64)
+        self.todo, self.ssd, self.late = (torch.empty((N * W,), **i64) for _ in range(3))
+        self.top = torch.empty((max(ram_slots - vram_slots, 1),), **i64)
+
+    def __call__(self, ram: ExpertTable, vram: ExpertTable, topk_ids: torch.Tensor,
+                 ram_base: int, working_base: int, top: torch.Tensor | None = None):
+        """Plan one step on the RAM table ``ram``; returns ``(need, cached_row, plan)`` with
+        ``plan = (dst_row, src_row, maps, todo, ssd, late)`` as ``plan_chunks`` returns it."""
+        native.require_cuda(topk_ids)
+        E = self.num_experts
+        if ram.num_experts != E or vram.num_experts != E:
+            raise ValueError("tables and plan must have the same number of experts")
+        ids, nb = _ids(topk_ids)
+        ntop = max(ram.num_slots - vram.num_slots, 1)
+        if top is not None:
+            top = top.to(device=self.device, dtype=torch.int64).contiguous()
+            if top.numel() != ntop:
+                raise ValueError(f"top must have {ntop} entries, got {top.numel()}")
+        cached_row = vram.slot_of[:E]
+        native.check(
+            native.lib().xp_plan_working(
+                ids.data_ptr(), nb, ids.numel(), E, *ram._table_args(),
+                vram.expert_in.data_ptr(), cached_row.data_ptr(), vram.num_slots, self.rows,
+                ram_base, working_base, native.ptr(top), self.top.data_ptr(),
+                self.need.data_ptr(), self.before.data_ptr(), self.dst_row.data_ptr(),
+                self.src_row.data_ptr(), self.maps.data_ptr(), self.todo.data_ptr(),
+                self.ssd.data_ptr(), self.late.data_ptr(), native.stream_of(self.device)),
+            "plan_working",
+        )
+        plan = (self.dst_row, self.src_row, self.maps, self.todo, self.ssd, self.late)
+        return self.need.view(torch.bool), cached_row, plan
