@@ -177,11 +177,15 @@ int xp_fetch(const int64_t *todo, int64_t K, const int64_t *row_of, int64_t base
  * no_cache, ...) without skip.  no_cache: int64[E] of -1.  scratch:
  * XP_STEP_SCRATCH_BYTES of device memory, 16-byte aligned, zeroed before the
  * first call and not shared by launches that may overlap; scratch word 3
- * (uint32) counts waits that gave up. */
+ * (uint32) counts waits that gave up.  topk_ids may be pinned host memory
+ * (read through the host link).  expert_map_host (may be NULL; no counterpart
+ * in the reference) is device-mapped pinned host memory that receives a copy
+ * of expert_map[E] from the kernel, so that a host-driven caller needs no
+ * copy-engine transfer per step. */
 int xp_decode_step(const void *topk_ids, int ids_bytes, int64_t K, int64_t E,
                    int64_t *a_slot_of, int64_t *a_expert_in, int64_t *a_last_used,
-                   int64_t *a_counters, int64_t a_slots, int32_t *expert_map, int64_t *a_slot,
-                   int64_t *a_todo,
+                   int64_t *a_counters, int64_t a_slots, int32_t *expert_map,
+                   int32_t *expert_map_host, int64_t *a_slot, int64_t *a_todo,
                    int64_t *b_slot_of, int64_t *b_expert_in, int64_t *b_last_used,
                    int64_t *b_counters, int64_t b_slots, int64_t *b_slot, int64_t *b_todo,
                    const int64_t *no_cache, int64_t base,

@@ -108,3 +108,43 @@ def test_fused_step_replays_in_a_cuda_graph(tmp_path):
         del graph
     finally:
         store.release()
+
+
+@pytest.mark.parametrize("compress,R", [(False, 32), (True, 16)], ids=["raw-ram", "compressed-ssd"])
+def test_host_ids_and_host_map_match_device_ids(tmp_path, compress, R):
+    """Pinned host ids (read by the kernel) and the kernel's host copy of expert_map
+    give the same step as device ids."""
+    from vllm_expert_pager import synthetic
+    from vllm_expert_pager.pager import PARAMS
+
+    experts = synthetic.fp8_experts_device(E, DEV, seed=5)
+    sa, host = build(tmp_path, "h", compress, R, experts)
+    sb, dev = build(tmp_path, "d", compress, R, experts)
+    try:
+        g = torch.Generator().manual_seed(11)
+        for step in range(30):
+            k = S if step % 4 else 5
+            ids_h = torch.randperm(E, generator=g)[:k].to(torch.int32).pin_memory()
+            map_h = torch.full((E,), -7, dtype=torch.int32).pin_memory()
+            ra = host.decode(ids_h, map_out=map_h)
+            rb = dev.decode(ids_h.to(DEV))
+            torch.cuda.synchronize()
+            assert torch.equal(ra.expert_map, rb.expert_map), step
+            assert torch.equal(map_h, rb.expert_map.cpu()), step
+            for t in ("vram", "ram"):
+                for attr in ("slot_of", "expert_in", "last_used", "counters"):
+                    assert torch.equal(getattr(getattr(host, t), attr),
+                                       getattr(getattr(dev, t), attr)), (step, t, attr)
+            for e in ids_h.tolist():
+                s = int(map_h[e])
+                for n in PARAMS:
+                    assert torch.equal(ra.slabs[n][s].view(torch.uint8),
+                                       experts[n][0][e].view(torch.uint8)), (step, e, n)
+        with pytest.raises(ValueError, match="pinned"):
+            host.decode(torch.zeros((1, S), dtype=torch.int32))
+        with pytest.raises(ValueError, match="map_out"):
+            host.decode(torch.zeros((1, S), dtype=torch.int32, device=DEV),
+                        map_out=torch.zeros(E, dtype=torch.int32))
+    finally:
+        sa.release()
+        sb.release()

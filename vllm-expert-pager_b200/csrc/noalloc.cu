@@ -90,7 +90,8 @@ extern "C" int xp_decode_step_noalloc(
   unsigned char *stg0 = compress ? scratch + kFlagsBytes : nullptr;
   unsigned char *stg1 = compress ? scratch + kFlagsBytes + stage0 : nullptr;
   rc = xp_decode_step(topk_ids, ids_bytes, K, E, a_slot_of, a_expert_in, a_last_used, a_counters,
-                      a_slots, expert_map, a_slot, a_todo, b_slot_of, b_expert_in, b_last_used,
+                      a_slots, expert_map, nullptr, a_slot, a_todo, b_slot_of, b_expert_in,
+                      b_last_used,
                       b_counters, b_slots, b_slot, b_todo, no_cache, base, src0, dst0, stg0, W0,
                       P0, src1, dst1, stg1, W1, P1, scale0, sdst0, SW0, scale1, sdst1, SW1,
                       compress, ctas, layer, seq, req, done, block, ring, retry_ns, giveup,

@@ -41,6 +41,7 @@ struct StepArgs {
   int64_t K, E;
   Table a, b;
   int32_t *map32;
+  int32_t *map_host;  // optional copy of expert_map in device-mapped host memory
   int64_t *a_slot, *a_todo, *b_slot, *b_todo;
   gdev::CopyJob ram, ssd;  // the two copy passes
   int copy_ctas;
@@ -99,6 +100,11 @@ __global__ void __launch_bounds__(gdev::kThreads) step_kernel(const __grid_const
     tdev::acquire_table(sm, t, p.E, p.K, vram ? p.map32 : nullptr, nullptr,
                         vram ? p.a_slot : p.b_slot, vram ? p.a_todo : p.b_todo, true, true);
     raise_flag(&flags[0]);
+    // The host copy of expert_map: written through the host link by the VRAM
+    // table's CTA after the copies are released (acquire_table ended with a
+    // barrier, so the map is complete).
+    if (vram && p.map_host)
+      for (int64_t e = threadIdx.x; e < p.E; e += blockDim.x) p.map_host[e] = p.map32[e];
   } else if (p.fetch && role == static_cast<int>(gridDim.x) - 1) {
     if (wait_flag(&flags[0], 2, p.table_wait_ns, &flags[3])) {
       gdev::fetch_publish(p.f);
@@ -137,7 +143,8 @@ using namespace xp;
 extern "C" int xp_decode_step(
     const void *topk_ids, int ids_bytes, int64_t K, int64_t E,
     int64_t *a_slot_of, int64_t *a_expert_in, int64_t *a_last_used, int64_t *a_counters,
-    int64_t a_slots, int32_t *expert_map, int64_t *a_slot, int64_t *a_todo,
+    int64_t a_slots, int32_t *expert_map, int32_t *expert_map_host, int64_t *a_slot,
+    int64_t *a_todo,
     int64_t *b_slot_of, int64_t *b_expert_in, int64_t *b_last_used, int64_t *b_counters,
     int64_t b_slots, int64_t *b_slot, int64_t *b_todo,
     const int64_t *no_cache, int64_t base,
@@ -155,6 +162,7 @@ extern "C" int xp_decode_step(
   p.a = Table{a_slot_of, a_expert_in, a_last_used, a_counters, a_slots};
   p.b = Table{b_slot_of, b_expert_in, b_last_used, b_counters, b_slots};
   p.map32 = expert_map;
+  p.map_host = expert_map_host;
   p.a_slot = a_slot;
   p.a_todo = a_todo;
   p.b_slot = b_slot;

@@ -45,7 +45,7 @@ _SIGNATURES = {
     "xp_fetch_wait": (_i32, [_p, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p]),
     "xp_fetch": (_i32, [_p, _i64, _p, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p]),
     "xp_decode_step": (_i32, [_p, _i32, _i64, _i64,
-                              _p, _p, _p, _p, _i64, _p, _p, _p,
+                              _p, _p, _p, _p, _i64, _p, _p, _p, _p,
                               _p, _p, _p, _p, _i64, _p, _p,
                               _p, _i64,
                               _p, _p, _p, _i64, _i64,

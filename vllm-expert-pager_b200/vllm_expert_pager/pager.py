@@ -131,7 +131,7 @@ class LayerPager:
     # ---- decode (experts.py:380-453) ----
 
     def decode(self, topk_ids: torch.Tensor, gather_events: list | None = None,
-               fused: bool = True) -> DecodeResult:
+               fused: bool = True, map_out: torch.Tensor | None = None) -> DecodeResult:
         """Page in this step's experts; returns the cache slab and expert_map.
 
         ``fused`` (default): one ``xp_decode_step`` launch does the table
@@ -140,9 +140,18 @@ class LayerPager:
         runs the reference's launch sequence (acquire, gather+fetch, decode,
         gather, decode).  ``gather_events``: if a list, a (start, end) pair of
         timing events around the copying launch is appended.
+
+        Host-driven callers (fused path): ``topk_ids`` may be a pinned host
+        tensor (int32 or int64, contiguous), which the kernel reads through the
+        host link, and ``map_out`` a pinned host int32 ``[E]`` tensor that the
+        kernel fills with this step's expert_map -- no copy-engine transfer per
+        step.  Neither buffer may be rewritten by the host before the step has
+        run on the GPU.
         """
         if fused:
-            return self._decode_fused(topk_ids, gather_events)
+            return self._decode_fused(topk_ids, gather_events, map_out)
+        if map_out is not None:
+            raise ValueError("map_out needs the fused decode step")
         store, layer = self.store, self.layer
         todo, ssd_todo = self.acquire(topk_ids)
         dst_row, src_row = self.acquire.vram_slot, self.acquire.ram_slot
@@ -171,14 +180,26 @@ class LayerPager:
             codec.decode_rows(ssd_todo, dst_row, cached_row, staging, self.cache_bytes, lut)
         return DecodeResult(self.cache_slab, self.expert_map)
 
-    def _decode_fused(self, topk_ids, gather_events=None) -> DecodeResult:
+    def _decode_fused(self, topk_ids, gather_events=None, map_out=None) -> DecodeResult:
         from vllm_expert_pager import gather as gather_mod
         from vllm_expert_pager import native
         from vllm_expert_pager.table import _ids
 
         store, layer = self.store, self.layer
-        native.require_cuda(topk_ids)
-        ids, nb = _ids(topk_ids)
+        if topk_ids.device.type == "cpu":
+            # Pinned host ids are read by the kernel through the host link (UVA).
+            ids = topk_ids.reshape(-1)
+            if not (ids.is_pinned() and ids.is_contiguous()
+                    and ids.dtype in (torch.int32, torch.int64)):
+                raise ValueError("host topk_ids must be pinned, contiguous int32/int64")
+            nb = ids.element_size()
+        else:
+            native.require_cuda(topk_ids)
+            ids, nb = _ids(topk_ids)
+        if map_out is not None and not (
+                map_out.device.type == "cpu" and map_out.is_pinned() and map_out.is_contiguous()
+                and map_out.dtype == torch.int32 and map_out.numel() == self.num_experts):
+            raise ValueError(f"map_out must be a pinned host int32 tensor of {self.num_experts}")
         K = ids.numel()
         pair, a, b = self.acquire, self.vram, self.ram
         staging = self.decode_staging
@@ -191,7 +212,8 @@ class LayerPager:
         native.check(
             native.lib().xp_decode_step(
                 ids.data_ptr(), nb, K, self.num_experts,
-                *a._table_args(), pair.expert_map.data_ptr(), pair.vram_slot.data_ptr(),
+                *a._table_args(), pair.expert_map.data_ptr(), native.ptr(map_out),
+                pair.vram_slot.data_ptr(),
                 pair._vram_todo.data_ptr(),
                 *b._table_args(), pair.ram_slot.data_ptr(), pair._ram_todo.data_ptr(),
                 a.no_cache.data_ptr(), layer * store.ram_slots,
