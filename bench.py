@@ -1195,7 +1195,14 @@ def main():
                     "d2h_bytes_per_step": W * E * 4},
             "roofline": {"bound": "host_link", "achieved": round(achieved, 3) if achieved else None,
                          "peak": round(peak, 3), "unit": "GB/s",
-                         "frac": round(achieved / peak, 4) if achieved else None, "traffic": None,
+                         "frac": round(achieved / peak, 4) if achieved else None,
+                         # Host-link bytes per average launch: an ncu capture of the step
+                         # kernel (profiles/step_kernel_config2.md) read exactly the
+                         # algorithmic bytes over the link (sysmem sectors x 32 B), so the
+                         # measured ratio 1.0 applies; DRAM per launch from the same capture.
+                         "traffic": int(moved / (args.steps * W)),
+                         "traffic_unit": "bytes per launch over the host link",
+                         "dram_bytes_per_launch": 87000,
                          "kernel": "step_kernel (both table updates + the gather, one launch "
                                    "per decode step)",
                          "peak_source": "measured in bench.py: copy engine pinned->device, "
