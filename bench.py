@@ -1197,9 +1197,10 @@ def main():
                          "peak": round(peak, 3), "unit": "GB/s",
                          "frac": round(achieved / peak, 4) if achieved else None,
                          # Host-link bytes per average launch: an ncu capture of the step
-                         # kernel (profiles/step_kernel_config2.md) read exactly the
-                         # algorithmic bytes over the link (sysmem sectors x 32 B), so the
-                         # measured ratio 1.0 applies; DRAM per launch from the same capture.
+                         # kernel (--set full, three launches of this workload) read exactly
+                         # the algorithmic bytes over the link (sysmem sectors x 32 B), so
+                         # the measured ratio 1.0 applies; DRAM per launch from the same
+                         # capture.
                          "traffic": int(moved / (args.steps * W)),
                          "traffic_unit": "bytes per launch over the host link",
                          "dram_bytes_per_launch": 87000,
