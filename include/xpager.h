@@ -285,6 +285,10 @@ void ssd_stop(void *server);
 void ssd_stats(void *server, long *fetches, long *reads, double *io_seconds, long *missed);
 const char *ssd_error(void *server);
 void ssd_test_delay(void *server, double seconds);
+/* No counterpart in the reference: the NUMA node whose CPUs the server's
+ * threads were bound to at ssd_start (the node holding pinned[0]'s first page,
+ * found with get_mempolicy), or -1 if the kernel did not report one. */
+int ssd_numa_node(void *server);
 
 #ifdef __cplusplus
 }

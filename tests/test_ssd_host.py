@@ -227,3 +227,34 @@ def test_random_sequence_matches_reference_server(tmp_path):
     finally:
         for ring in rings:
             ring.close()
+
+
+def test_threads_bound_to_the_ram_tier_node(tmp_path):
+    """The server runs on the CPUs of the NUMA node holding the RAM tier (or stays
+    unbound when the kernel reports no node), and still serves requests."""
+    so = native.lib()
+    r = Ring(so, tmp_path, L=1, E=8, R=4)
+    try:
+        node = so.ssd_numa_node(ctypes.c_void_p(r.h))
+        nodes = sorted(int(d[4:]) for d in os.listdir("/sys/devices/system/node")
+                       if d.startswith("node") and d[4:].isdigit()) \
+            if os.path.isdir("/sys/devices/system/node") else []
+        assert node == -1 or node in nodes
+        if node >= 0:
+            with open(f"/sys/devices/system/node/node{node}/cpulist") as f:
+                want = f.read().strip()
+            lists = []
+            for tid in os.listdir("/proc/self/task"):
+                try:
+                    with open(f"/proc/self/task/{tid}/status") as f:
+                        lists += [ln.split(":", 1)[1].strip() for ln in f
+                                  if ln.startswith("Cpus_allowed_list")]
+                except OSError:
+                    pass
+            assert want in lists  # at least the server and worker threads
+        seq = r.publish(0, [3], [1])
+        r.wait(seq)
+        assert np.array_equal(r.row(0, 1), r.expected(0, 0, 3))
+    finally:
+        r.close()
+    assert so.ssd_numa_node(None) == -1

@@ -7,7 +7,8 @@
 // with the heap's tie order, the canonical bit-reversed codes of codec.py:90-114,
 // and the Huffman words of each group in refill order (codec.py:150-181).
 //
-// Five launches per batch of rows, all on the caller's stream, no allocation:
+// A scratch clear and five launches per batch of rows, all on the caller's
+// stream, no allocation:
 //   1. hist   exponent histogram per row (packed 8-bit counters per thread);
 //   2. code   code lengths + canonical codes + LUT, one warp per row;
 //   3. count  Huffman words per group (sum of the lanes' refill counts);
@@ -372,11 +373,9 @@ extern "C" int xp_encode_rows(const void *raw, int64_t rows, int64_t n, int64_t 
             static_cast<uint8_t *>(records), static_cast<uint8_t *>(luts), used,
             static_cast<unsigned char *>(scratch)};
   cudaStream_t s = as_stream(stream);
-  for (int64_t r = 0; r < rows; ++r) {
-    cudaError_t err = cudaMemsetAsync(static_cast<unsigned char *>(scratch) + r * row_scratch_bytes(G),
-                                      0, 64, s);
-    if (err != cudaSuccess) return static_cast<int>(err);
-  }
+  // One clear of the batch's scratch (the histograms accumulate by atomics).
+  cudaError_t err = cudaMemsetAsync(scratch, 0, static_cast<size_t>(rows * row_scratch_bytes(G)), s);
+  if (err != cudaSuccess) return static_cast<int>(err);
   enc_hist_kernel<<<dim3(kHistBlocksPerRow, static_cast<unsigned>(rows)), kHistThreads, 0, s>>>(a);
   enc_code_kernel<<<static_cast<unsigned>(rows), 32, 0, s>>>(a);
   const unsigned gb = static_cast<unsigned>((G + kWarpsPerBlock - 1) / kWarpsPerBlock);

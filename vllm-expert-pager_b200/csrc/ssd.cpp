@@ -15,14 +15,18 @@
 //
 // Implementation: one server thread spinning on the ring (a sleep adds ~100 us
 // to the round trip) and a pool of worker threads that take the request's jobs
-// one at a time under a mutex (a job is a multi-megabyte read).
+// one at a time under a mutex (a job is a multi-megabyte read).  All of them
+// run on the CPUs of the NUMA node that holds the RAM tier.
 #define _GNU_SOURCE 1
 #include <errno.h>
+#include <pthread.h>
 #include <sched.h>
 #include <stdarg.h>
 #include <stdint.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
+#include <sys/syscall.h>
 #include <sys/uio.h>
 #include <time.h>
 #include <unistd.h>
@@ -62,8 +66,46 @@ inline void cpu_relax(long &spins) {
 int64_t load_acq(const volatile int64_t *p) { return __atomic_load_n(p, __ATOMIC_ACQUIRE); }
 void store_rel(volatile int64_t *p, int64_t v) { __atomic_store_n(p, v, __ATOMIC_RELEASE); }
 
+// NUMA node of the page at addr (get_mempolicy(2) with MPOL_F_NODE |
+// MPOL_F_ADDR, spelled out to avoid libnuma), -1 if the kernel does not say.
+int node_of(const void *addr) {
+  constexpr unsigned long kNode = 1ul << 0, kAddr = 1ul << 1;
+  int node = -1;
+  const long rc = syscall(SYS_get_mempolicy, &node, nullptr, 0ul, addr, kNode | kAddr);
+  return rc == 0 ? node : -1;
+}
+
+// CPUs of a NUMA node from sysfs ("0-15,32-47"); false if unreadable or empty.
+bool node_cpus(int node, cpu_set_t *set) {
+  char path[96];
+  snprintf(path, sizeof path, "/sys/devices/system/node/node%d/cpulist", node);
+  FILE *f = fopen(path, "r");
+  if (!f) return false;
+  char buf[4096];
+  const bool got = fgets(buf, sizeof buf, f) != nullptr;
+  fclose(f);
+  if (!got) return false;
+  CPU_ZERO(set);
+  int count = 0;
+  for (char *p = buf; *p && *p != '\n';) {
+    char *end;
+    long a = strtol(p, &end, 10);
+    if (end == p) return false;
+    long b = a;
+    if (*end == '-') {
+      p = end + 1;
+      b = strtol(p, &end, 10);
+      if (end == p) return false;
+    }
+    for (long c = a; c <= b && c < CPU_SETSIZE; ++c, ++count) CPU_SET(static_cast<int>(c), set);
+    p = *end == ',' ? end + 1 : end;
+  }
+  return count > 0;
+}
+
 struct Server {
   int fd;
+  int numa_node = -1;  // node the threads are bound to, -1 if not bound
   volatile int64_t *req, *done;
   long ring, block, slot_words, L, E, rows, record_bytes;
   int names;
@@ -239,7 +281,22 @@ extern "C" void *ssd_start(int fd, void *req, void *done, long ring, long block,
   s->job_row.assign(static_cast<size_t>(block), 0);
   for (int i = 0; i < nworkers; ++i) s->workers.emplace_back([s] { s->worker_main(); });
   s->server = std::thread([s] { s->server_main(); });
+  // The reads land in the RAM tier: run the server and its workers on the CPUs
+  // of the NUMA node that holds it (the GPU's node, where the tier is placed).
+  const int node = node_of(s->pinned[0]);
+  cpu_set_t set;
+  if (node >= 0 && node_cpus(node, &set)) {
+    bool ok = pthread_setaffinity_np(s->server.native_handle(), sizeof set, &set) == 0;
+    for (auto &t : s->workers)
+      ok = pthread_setaffinity_np(t.native_handle(), sizeof set, &set) == 0 && ok;
+    if (ok) s->numa_node = node;
+  }
   return s;
+}
+
+extern "C" int ssd_numa_node(void *server) {
+  const Server *s = static_cast<const Server *>(server);
+  return s ? s->numa_node : -1;
 }
 
 extern "C" void ssd_stop(void *server) {

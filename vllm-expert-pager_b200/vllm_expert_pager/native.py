@@ -75,6 +75,7 @@ _SIGNATURES = {
                          ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_long)]),
     "ssd_error": (ctypes.c_char_p, [_p]),
     "ssd_test_delay": (None, [_p, ctypes.c_double]),
+    "ssd_numa_node": (_i32, [_p]),
 }
 
 XP_OK = 0
