@@ -581,6 +581,47 @@ def run_prefill(args, device, path) -> dict:
     return out
 
 
+def disk_peak(path: str, record_bytes: int, seconds: float = 3.0) -> dict:
+    """Raw read bandwidth of the paging file: random whole records with O_DIRECT
+    preadv into page-aligned buffers, from 8 and from 32 threads for ``seconds``
+    each (the server's reads are record-sized preadv's too); the better of the two."""
+    import mmap
+    import random
+    import threading
+
+    size = os.path.getsize(path)
+    n = size // record_bytes
+    best = None
+    for threads in (8, 32):
+        try:
+            fd = os.open(path, os.O_RDONLY | os.O_DIRECT)
+        except OSError:
+            return {"unavailable": "O_DIRECT open failed"}
+        total = [0] * threads
+        stop = time.perf_counter() + seconds
+
+        def reader(i):
+            buf = mmap.mmap(-1, record_bytes)
+            rng = random.Random(i)
+            while time.perf_counter() < stop:
+                total[i] += os.preadv(fd, [buf], rng.randrange(n) * record_bytes)
+            buf.close()
+
+        t0 = time.perf_counter()
+        ts = [threading.Thread(target=reader, args=(i,)) for i in range(threads)]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join()
+        dt = time.perf_counter() - t0
+        os.close(fd)
+        gbs = sum(total) / dt / 1e9
+        if best is None or gbs > best["gb_per_s"]:
+            best = {"gb_per_s": round(gbs, 3), "threads": threads}
+    best["how"] = "random record-sized O_DIRECT preadv on the paging file, 8 or 32 threads"
+    return best
+
+
 def run_model_workload(args):
     """--workload model|compressed|prefill: configs 3, 4 and 5 (one JSON line each)."""
     world, rank, local = dist_setup()
@@ -597,6 +638,22 @@ def run_model_workload(args):
                                                       max(args.tokens // 4, 8), path)}
         else:
             res = {"config5": run_prefill(args, device, path)}
+        if os.path.exists(path):
+            from vllm_expert_pager import synthetic
+            from vllm_expert_pager.codec import pitch_of
+
+            record = sum(pitch_of(r * c, 0.89, 4096) for r, c in synthetic.SHAPES.values())
+            peak = disk_peak(path, record)
+
+            def annotate(d):
+                for v in d.values():
+                    if isinstance(v, dict):
+                        annotate(v)
+                if "ssd_gb_per_s" in d and "gb_per_s" in peak:
+                    d["ssd_frac_of_disk_peak"] = round(d["ssd_gb_per_s"] / peak["gb_per_s"], 3)
+
+            annotate(res)
+            res["disk_peak"] = peak
     finally:
         if os.path.exists(path):
             os.unlink(path)
