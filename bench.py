@@ -743,7 +743,7 @@ def codec_baselines(device) -> dict:
     * ``cpu_decode_port``: the reference's sequential decoder restated in C
       (oracle/decode.c) on all host threads;
     * ``native_encode``: this library's encoder (host, load time), all threads;
-    * ``gpu_decode``: decode_kernel on the same 16 records (8 rows per launch
+    * ``gpu_decode``: decode_ring_kernel on the same 16 records (8 rows per launch
       per name, 2 launches).
     All values are raw MB/s; every round trip is checked byte for byte.
     """
