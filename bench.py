@@ -582,43 +582,51 @@ def run_prefill(args, device, path) -> dict:
 
 
 def disk_peak(path: str, record_bytes: int, seconds: float = 3.0) -> dict:
-    """Raw read bandwidth of the paging file: random whole records with O_DIRECT
-    preadv into page-aligned buffers, from 8 and from 32 threads for ``seconds``
-    each (the server's reads are record-sized preadv's too); the better of the two."""
+    """Raw read bandwidth of the paging file: random O_DIRECT preadv's into
+    page-aligned buffers, of whole records and of the server's read-job size
+    (512 KiB chunks at record offsets), from 8 and from 32 threads for ``seconds``
+    each; the best of the four."""
     import mmap
     import random
     import threading
 
+    from vllm_expert_pager import store as store_mod
+
     size = os.path.getsize(path)
     n = size // record_bytes
+    chunk = store_mod._READ_CHUNK if 0 < store_mod._READ_CHUNK < record_bytes else record_bytes
     best = None
-    for threads in (8, 32):
-        try:
-            fd = os.open(path, os.O_RDONLY | os.O_DIRECT)
-        except OSError:
-            return {"unavailable": "O_DIRECT open failed"}
-        total = [0] * threads
-        stop = time.perf_counter() + seconds
+    for nbytes in sorted({record_bytes, chunk // 4096 * 4096}):
+        for threads in (8, 32):
+            try:
+                fd = os.open(path, os.O_RDONLY | os.O_DIRECT)
+            except OSError:
+                return {"unavailable": "O_DIRECT open failed"}
+            total = [0] * threads
+            stop = time.perf_counter() + seconds
 
-        def reader(i):
-            buf = mmap.mmap(-1, record_bytes)
-            rng = random.Random(i)
-            while time.perf_counter() < stop:
-                total[i] += os.preadv(fd, [buf], rng.randrange(n) * record_bytes)
-            buf.close()
+            def reader(i):
+                buf = mmap.mmap(-1, nbytes)
+                rng = random.Random(i)
+                pieces = record_bytes // nbytes
+                while time.perf_counter() < stop:
+                    off = rng.randrange(n) * record_bytes + rng.randrange(pieces) * nbytes
+                    total[i] += os.preadv(fd, [buf], off)
+                buf.close()
 
-        t0 = time.perf_counter()
-        ts = [threading.Thread(target=reader, args=(i,)) for i in range(threads)]
-        for t in ts:
-            t.start()
-        for t in ts:
-            t.join()
-        dt = time.perf_counter() - t0
-        os.close(fd)
-        gbs = sum(total) / dt / 1e9
-        if best is None or gbs > best["gb_per_s"]:
-            best = {"gb_per_s": round(gbs, 3), "threads": threads}
-    best["how"] = "random record-sized O_DIRECT preadv on the paging file, 8 or 32 threads"
+            t0 = time.perf_counter()
+            ts = [threading.Thread(target=reader, args=(i,)) for i in range(threads)]
+            for t in ts:
+                t.start()
+            for t in ts:
+                t.join()
+            dt = time.perf_counter() - t0
+            os.close(fd)
+            gbs = sum(total) / dt / 1e9
+            if best is None or gbs > best["gb_per_s"]:
+                best = {"gb_per_s": round(gbs, 3), "threads": threads, "read_bytes": nbytes}
+    best["how"] = ("random O_DIRECT preadv on the paging file, whole records or the server's "
+                   "read-job size, 8 or 32 threads; the best")
     return best
 
 

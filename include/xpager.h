@@ -289,6 +289,12 @@ void ssd_test_delay(void *server, double seconds);
  * threads were bound to at ssd_start (the node holding pinned[0]'s first page,
  * found with get_mempolicy), or -1 if the kernel did not report one. */
 int ssd_numa_node(void *server);
+/* No counterpart in the reference: split every record read of later requests
+ * into jobs of `bytes` (rounded down to whole 4 KiB pages; 0, or at least
+ * record_bytes: one job per record, the reference's behaviour), read by the
+ * server's threads concurrently.  A request of one or two experts then keeps
+ * nworkers+1 reads in flight instead of one or two. */
+void ssd_set_read_chunk(void *server, long bytes);
 
 #ifdef __cplusplus
 }

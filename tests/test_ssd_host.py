@@ -54,15 +54,16 @@ def aligned(nbytes: int) -> np.ndarray:
 class Ring:
     """The pinned ring, RAM-tier rows and paging file of one server instance."""
 
-    def __init__(self, so, tmp_path, L, E, R, working=2, workers=7):
+    def __init__(self, so, tmp_path, L, E, R, working=2, workers=7, pitch=PITCH):
         self.so, self.L, self.E, self.R = so, L, E, R
+        self.pitch = tuple(pitch)
         self.block = 1 << (E - 1).bit_length()
         self.slot_words = 2 + 2 * self.block
         self.req = np.zeros(2 + RING * self.slot_words, dtype=np.int64)
         self.done = np.zeros(1, dtype=np.int64)
         self.rows = L * R + working
-        self.record = sum(PITCH)
-        self.pinned = [aligned(self.rows * p) for p in PITCH]
+        self.record = sum(self.pitch)
+        self.pinned = [aligned(self.rows * p) for p in self.pitch]
         rng = np.random.default_rng(L * 1000 + E)
         self.file = rng.integers(0, 256, L * E * self.record, dtype=np.uint8)
         path = str(tmp_path / f"pager-{id(self)}.bin")
@@ -72,7 +73,7 @@ class Ring:
         except OSError:
             self.fd = os.open(path, os.O_RDONLY)
         ptrs = (ctypes.c_void_p * 2)(*(p.ctypes.data for p in self.pinned))
-        pitch = (ctypes.c_long * 2)(*PITCH)
+        pitch = (ctypes.c_long * 2)(*self.pitch)
         self.h = so.ssd_start(self.fd, ctypes.c_void_p(self.req.ctypes.data),
                               ctypes.c_void_p(self.done.ctypes.data), RING, self.block, L, E,
                               self.rows, self.record, 2, ptrs, pitch, workers)
@@ -108,12 +109,12 @@ class Ring:
         return None if e is None else e.decode()
 
     def row(self, k, row):
-        p = PITCH[k]
+        p = self.pitch[k]
         return self.pinned[k][row * p : (row + 1) * p]
 
     def expected(self, k, layer, e):
-        off = (layer * self.E + e) * self.record + sum(PITCH[:k])
-        return self.file[off : off + PITCH[k]]
+        off = (layer * self.E + e) * self.record + sum(self.pitch[:k])
+        return self.file[off : off + self.pitch[k]]
 
     def close(self):
         self.so.ssd_stop(ctypes.c_void_p(self.h))
@@ -258,3 +259,43 @@ def test_threads_bound_to_the_ram_tier_node(tmp_path):
     finally:
         r.close()
     assert so.ssd_numa_node(None) == -1
+
+
+@pytest.mark.parametrize("chunk", [0, 4096, 5000, 8192, 12288, 20480, 1 << 20])
+def test_chunked_reads_fill_the_same_rows(tmp_path, chunk):
+    """ssd_set_read_chunk splits each record read into page-aligned jobs (a chunk of
+    8192 B spans the two names' pieces of a 20480-B record; 5000 B rounds down to
+    one page; 0 and sizes of a record or more read whole records): the RAM-tier rows,
+    done and the statistics (reads count records) are those of whole-record reads."""
+    so = native.lib()
+    r = Ring(so, tmp_path, L=2, E=16, R=8, pitch=(12288, 8192))
+    try:
+        so.ssd_set_read_chunk(ctypes.c_void_p(r.h), chunk)
+        rng = np.random.default_rng(chunk)
+        for _ in range(12):
+            layer = int(rng.integers(0, 2))
+            n = int(rng.integers(1, 6))
+            experts = rng.choice(16, n, replace=False).tolist()
+            rows = rng.choice(2 * 8 + 2, n, replace=False).tolist()
+            r.wait(r.publish(layer, experts, rows))
+            for e, row in zip(experts, rows):
+                for k in range(2):
+                    assert np.array_equal(r.row(k, row), r.expected(k, layer, e))
+        assert r.stats()[0] == 12 and r.error() is None
+    finally:
+        r.close()
+
+
+def test_chunked_read_failure_still_writes_done(tmp_path):
+    """A chunked request whose row is outside the RAM tier reports the error once and
+    still completes (done = seq); the request's other expert is read."""
+    so = native.lib()
+    r = Ring(so, tmp_path, L=2, E=8, R=4, pitch=(12288, 8192))
+    try:
+        so.ssd_set_read_chunk(ctypes.c_void_p(r.h), 4096)
+        r.wait(r.publish(1, [4, 5], [10**6, 0]))
+        assert r.error() is not None and "outside the RAM tier" in r.error()
+        for k in range(2):
+            assert np.array_equal(r.row(k, 0), r.expected(k, 1, 5))
+    finally:
+        r.close()

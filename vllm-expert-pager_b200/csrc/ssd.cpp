@@ -15,8 +15,12 @@
 //
 // Implementation: one server thread spinning on the ring (a sleep adds ~100 us
 // to the round trip) and a pool of worker threads that take the request's jobs
-// one at a time under a mutex (a job is a multi-megabyte read).  All of them
-// run on the CPUs of the NUMA node that holds the RAM tier.
+// one at a time under a mutex (a job is a read of hundreds of kilobytes to a
+// few megabytes).  All of them run on the CPUs of the NUMA node that holds the
+// RAM tier.  A job is one record, or, when ssd_set_read_chunk set a chunk size,
+// one page-aligned chunk of a record: a request of one or two experts then
+// keeps every reader busy instead of one or two (a disk reaches its bandwidth
+// only with several reads in flight).
 #define _GNU_SOURCE 1
 #include <errno.h>
 #include <pthread.h>
@@ -118,6 +122,7 @@ struct Server {
   char err[512];
   std::atomic<int> failing{0}, failed{0};
   std::atomic<double> test_delay{0.0};
+  std::atomic<long> read_chunk{0};  // bytes per job, 0: whole records
 
   // the current request's jobs
   long layer = 0;
@@ -125,6 +130,7 @@ struct Server {
   // Taking a job and counting it finished happen under mu, so a worker that
   // wakes up late cannot pair an index of one request with another's count.
   long njobs = 0, next = 0;
+  long chunk = 0, per_record = 1;  // this request's job size and jobs per record
   std::atomic<long> finished{0};
   std::mutex mu;
   std::condition_variable cv;
@@ -143,8 +149,12 @@ struct Server {
     failed.store(1, std::memory_order_release);
   }
 
+  // Job j: bytes [lo, hi) of record j / per_record, lo = (j % per_record) * chunk.
+  // The record is the names' pieces back to back (pitch[0] bytes of name 0,
+  // then name 1, ...), each read into the row's pinned piece of that name.
   void read_one(long j) {
-    const long e = job_expert[j], row = job_row[j];
+    const long r = j / per_record;
+    const long e = job_expert[r], row = job_row[r];
     if (layer < 0 || layer >= L || e < 0 || e >= E) {
       fail("expert %ld of layer %ld is out of range", e, layer);
       return;
@@ -154,17 +164,27 @@ struct Server {
            layer, rows);
       return;
     }
+    const long lo = (j % per_record) * chunk;
+    const long hi = lo + chunk < record_bytes ? lo + chunk : record_bytes;
     iovec iov[kMaxNames];
+    int k = 0;
+    long base = 0;
     for (int i = 0; i < names; ++i) {
-      iov[i].iov_base = pinned[i] + row * pitch[i];
-      iov[i].iov_len = static_cast<size_t>(pitch[i]);
+      const long a = lo > base ? lo : base, b = hi < base + pitch[i] ? hi : base + pitch[i];
+      if (a < b) {
+        iov[k].iov_base = pinned[i] + row * pitch[i] + (a - base);
+        iov[k].iov_len = static_cast<size_t>(b - a);
+        ++k;
+      }
+      base += pitch[i];
     }
-    const off_t off = static_cast<off_t>(layer * E + e) * record_bytes;
-    ssize_t n = preadv(fd, iov, names, off);
+    const off_t off = static_cast<off_t>(layer * E + e) * record_bytes + lo;
+    ssize_t n = preadv(fd, iov, k, off);
     if (n < 0)
       fail("preadv of expert %ld of layer %ld failed: %s", e, layer, strerror(errno));
-    else if (n != record_bytes)
-      fail("short read: %zd of %ld B for expert %ld of layer %ld", n, record_bytes, e, layer);
+    else if (n != hi - lo)
+      fail("short read: %zd of %ld B at byte %ld of expert %ld of layer %ld", n, hi - lo, lo, e,
+           layer);
   }
 
   void run_jobs() {
@@ -230,17 +250,25 @@ struct Server {
           job_row[n] = static_cast<long>(slot[2 + block + j]);
           ++n;
         }
-        njobs = n;
+        // Chunks are whole pages (O_DIRECT), and only used when the record is
+        // exactly the names' pieces (always, for records written by Store).
+        long c = read_chunk.load(std::memory_order_relaxed) / 4096 * 4096;
+        long sum = 0;
+        for (int i = 0; i < names; ++i) sum += pitch[i];
+        if (c <= 0 || c >= record_bytes || sum != record_bytes) c = record_bytes;
+        chunk = c;
+        per_record = (record_bytes + c - 1) / c;
+        njobs = n * per_record;
         next = 0;
         finished.store(0, std::memory_order_release);
-        if (n > 1 && !workers.empty()) {  // a single job is read here without waking anyone
+        if (njobs > 1 && !workers.empty()) {  // a single job is read here without waking anyone
           ++gen;
           cv.notify_all();
         }
       }
       run_jobs();
       spins = 0;
-      while (finished.load(std::memory_order_acquire) < n) cpu_relax(spins);
+      while (finished.load(std::memory_order_acquire) < n * per_record) cpu_relax(spins);
       fetches.fetch_add(1);
       reads.fetch_add(n);
       io_seconds.store(io_seconds.load() + (now_s() - t0));
@@ -324,6 +352,10 @@ extern "C" void ssd_stats(void *server, long *fetches, long *reads, double *io_s
 extern "C" const char *ssd_error(void *server) {
   Server *s = static_cast<Server *>(server);
   return s->failed.load(std::memory_order_acquire) ? s->err : nullptr;
+}
+
+extern "C" void ssd_set_read_chunk(void *server, long bytes) {
+  static_cast<Server *>(server)->read_chunk.store(bytes < 0 ? 0 : bytes, std::memory_order_relaxed);
 }
 
 extern "C" void ssd_test_delay(void *server, double seconds) {

@@ -76,6 +76,7 @@ _SIGNATURES = {
     "ssd_error": (ctypes.c_char_p, [_p]),
     "ssd_test_delay": (None, [_p, ctypes.c_double]),
     "ssd_numa_node": (_i32, [_p]),
+    "ssd_set_read_chunk": (None, [_p, _long]),
 }
 
 XP_OK = 0

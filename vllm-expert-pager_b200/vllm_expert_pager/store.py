@@ -44,6 +44,11 @@ _ALIGN = 4096
 # NVMe saturating at 8 outstanding reads.  VLLM_EXPERT_PAGER_READ_WORKERS sets
 # it for devices that want a deeper queue.
 _READ_WORKERS = max(1, int(os.environ.get("VLLM_EXPERT_PAGER_READ_WORKERS", "8")))
+# Bytes per read job of the SSD server (whole 4 KiB pages): each record read is
+# split into jobs of this size that the read threads take concurrently, so a
+# request of one or two experts keeps all of them busy.  0 reads whole records,
+# one per thread, as the reference does.  VLLM_EXPERT_PAGER_READ_CHUNK sets it.
+_READ_CHUNK = max(0, int(os.environ.get("VLLM_EXPERT_PAGER_READ_CHUNK", str(512 << 10))))
 # Slots in the request ring (store.py:65-67).
 RING = 4
 # GPU wait for the host: re-publish every RETRY_NS, give up after GIVEUP
@@ -219,6 +224,7 @@ class Store:
         )  # fmt: skip
         if not self._handle:
             raise RuntimeError("vllm-expert-pager: cannot start the SSD server")
+        self._so.ssd_set_read_chunk(ctypes.c_void_p(self._handle), _READ_CHUNK)
 
     def close(self) -> None:
         """Stop the host server and release the pinned memory and files."""
