@@ -31,6 +31,8 @@
 //    step.
 //  * Each lane stores 16 bytes per 16 symbols; nibble words are loaded two
 //    iterations ahead and prefetched into L2 eight iterations ahead.
+#include <atomic>
+
 #include "common.cuh"
 
 namespace xp {
@@ -426,16 +428,17 @@ extern "C" int xp_decode_rows(const int64_t *todo, int64_t K, const int64_t *dst
   const int64_t groups = a.n[0].G + a.n[1].G;
   // Launches of at most 12 warps per SM are latency-bound (three warps or
   // fewer per scheduler): they take the pipelined step.
-  static int sm_count[64];
+  static std::atomic<int> sm_count[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return XP_EINVAL;
-  if (sm_count[dev] == 0) {
-    int n = 0;
-    cudaError_t err = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  int sms = sm_count[dev].load(std::memory_order_relaxed);
+  if (sms == 0) {
+    cudaError_t err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (err != cudaSuccess) return static_cast<int>(err);
-    sm_count[dev] = n > 0 ? n : 1;
+    sms = sms > 0 ? sms : 1;
+    sm_count[dev].store(sms, std::memory_order_relaxed);
   }
-  const bool piped = K * groups <= int64_t(12) * sm_count[dev];
+  const bool piped = K * groups <= int64_t(12) * sms;
   dim3 grid(static_cast<unsigned>((groups + kWarps - 1) / kWarps), static_cast<unsigned>(K));
   auto kern = piped ? decode_ring_kernel<true> : decode_ring_kernel<false>;
   kern<<<grid, kWarps * 32, kRingSmem, as_stream(stream)>>>(a);
