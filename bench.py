@@ -247,8 +247,8 @@ def hbm_peak() -> tuple[float, str]:
         return 6650.0, "fallback 6.65 TB/s (no MEASURED_PEAKS.json)"
 
 
-def bench_decode(device, rows_per_launch: int, launches: int = 24, distinct: int = 64,
-                 reps: int = 3) -> dict:
+def bench_decode(device, rows_per_launch: int, launches: int = 48, distinct: int = 64,
+                 reps: int = 5) -> dict:
     """Decode kernel alone: compressed config-1 experts staged in HBM -> raw slab rows.
 
     ``distinct`` experts (encoded at pitch 0.89 with the native encoder) sit in a
@@ -289,27 +289,39 @@ def bench_decode(device, rows_per_launch: int, launches: int = 24, distinct: int
     ident = torch.arange(distinct, dtype=torch.int64, device=device)
     no_cache = torch.full((distinct,), -1, dtype=torch.int64, device=device)
 
+    views = [[x[s0 : s0 + K] for x in stg] for s0 in starts]
+
     def launch(i):
         # launch i expands experts [s0, s0+K): staging row j holds expert s0+j, whose
         # raw row goes to dst row s0+j (dst_row = identity)
-        s0 = starts[i % len(starts)]
-        codec.decode_rows(todos[i % len(starts)], ident, no_cache,
-                          [x[s0 : s0 + K] for x in stg], dst, lut_d)
+        j = i % len(starts)
+        codec.decode_rows(todos[j], ident, no_cache, views[j], dst, lut_d)
 
     for i in range(4):
         launch(i)
     torch.cuda.synchronize()
+    # The launches are captured in a CUDA graph and timed by replaying it between
+    # two events on its stream: per-launch events around a Python call would also
+    # count the host's launch time whenever that exceeds the kernel's (small K).
+    s = torch.cuda.Stream(device=device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(s):
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            for i in range(launches):
+                launch(i)
+    torch.cuda.synchronize()
     best = None
     for _ in range(reps):
-        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-              for _ in range(launches)]
-        for i in range(launches):
-            ev[i][0].record()
-            launch(i)
-            ev[i][1].record()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s):
+            a.record()
+            graph.replay()
+            b.record()
         torch.cuda.synchronize()
-        us = sum(a.elapsed_time(b) for a, b in ev) * 1e3 / launches
+        us = a.elapsed_time(b) * 1e3 / launches
         best = us if best is None else min(best, us)
+    del graph
     for n, d, k in zip(names, dst, range(2)):  # parity spot check: expanded rows == raw rows
         for e in range(0, distinct, 17):
             if not torch.equal(d[e].cpu(), recs[n][e][1]):

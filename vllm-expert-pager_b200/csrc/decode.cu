@@ -17,22 +17,21 @@
 //    read consecutive words (ballot + popc give each its slot), one
 //    conflict-free shared load.  The ring (instead of staging a whole group,
 //    ~7.3 KiB) lets 10 CTAs share an SM.
-//  * One unconditional lookup in the 512-byte LUT per symbol (the table is
-//    512-byte aligned, so its address is one AND/OR of the window).
-//  * The kernel is bound by the integer ALU pipe (half rate: one warp
-//    instruction per two cycles per scheduler) and, in small launches, by the
-//    symbol-to-symbol dependency chain.  Exponent bits of 4 symbols are summed
-//    with multiply-adds and sign/mantissa nibbles spread with multiplies, both on
-//    the FMA pipe; one select merges them.
-//  * Small launches (at most 12 warps per SM) decide each symbol's refill one
-//    symbol early from a length-only lookup of the pre-insert buffer, which
-//    takes the ballot -> word-load latency off the per-symbol chain at the cost
-//    of a second lookup; larger launches are throughput-bound and use the plain
-//    step.
+//  * Two symbols per ballot round (step_pair): a lane refills at most once in
+//    two consecutive symbols, its refill time follows from a length-only
+//    lookup of its current buffer, and its word can be inserted above its
+//    valid bits before the first of the two; so one round of two ballots and
+//    one word load serves two symbols, which halves the refill work on the
+//    symbol-to-symbol chain.
+//  * One lookup in the 512-byte LUT per symbol (the table is 512-byte aligned,
+//    so its address is one AND/OR of the window).
+//  * Every instruction is integer work; the integer ALU pipe (one warp
+//    instruction per two cycles per scheduler) is the busiest unit in large
+//    launches.  Exponent bits of 4 symbols are summed with multiply-adds and
+//    sign/mantissa nibbles spread with multiplies, both on the FMA pipe; one
+//    select merges them.
 //  * Each lane stores 16 bytes per 16 symbols; nibble words are loaded two
 //    iterations ahead and prefetched into L2 eight iterations ahead.
-#include <atomic>
-
 #include "common.cuh"
 
 namespace xp {
@@ -159,91 +158,68 @@ constexpr uint32_t kRing = 4096, kHalf = 2048;
 // Dynamic shared memory per CTA: kWarps rings plus the slack that aligns them.
 constexpr size_t kRingSmem = kWarps * kRing + kRing;
 
-// One symbol step with ring-addressed refills.  nv = 8 - level: this symbol
-// refills iff nv >= 0, and 0x100 >> nv is then 1 << level (0 otherwise: the
-// shift count of a negative nv is clamped to 32), the multiplier that places
-// the new word above the buffer's valid bits.  off is the byte offset of the
-// next unread word in the group's stream (the ring slot is off mod 4 KiB).
-__device__ __forceinline__ uint32_t step_ring(uint64_t &buf, int &nv, uint32_t &off,
-                                              uint32_t base, uint32_t lut, unsigned lt) {
-  uint32_t ent;
+// Two symbols per ballot round.  A lane that refills at symbol i cannot refill
+// at i+1 (the refill leaves at least 23 bits after symbol i), so each lane
+// refills at most once per pair, at i (level < 9) or at i+1 (level >= 9 and
+// level - len_i < 9, len_i from a length-only lookup of the current buffer,
+// which holds level >= 9 valid bits).  Two ballots order the pair's refills as
+// the format does (all of symbol i's in lane order, then symbol i+1's), one
+// shared load gives each refilling lane its word, and the word is inserted
+// right above the lane's valid bits before symbol i: for a lane refilling at
+// i+1 that is where the format puts it after symbol i's bits are consumed, and
+// symbol i reads only bits below it.  The insert position is at most 23 bits,
+// so the 64-bit buffer holds it; its multiplier 0x800000 >> (nv + 15) is
+// 1 << level for level <= 23.  Returns the two LUT entries.
+__device__ __forceinline__ void step_pair(uint64_t &buf, int &nv, uint32_t &off, uint32_t base,
+                                          uint32_t lut, uint32_t lenlut, unsigned lt,
+                                          uint32_t &e0, uint32_t &e1) {
   asm volatile(
       "{\n\t"
-      ".reg .pred p;\n\t"
-      ".reg .b32 bal, t, c, a, w, m, n, x, len;\n\t"
-      "setp.ge.s32 p, %1, 0;\n\t"
-      "vote.sync.ballot.b32 bal, p, 0xffffffff;\n\t"
-      "and.b32 t, bal, %4;\n\t"
-      "popc.b32 c, t;\n\t"
-      "mad.lo.u32 a, c, 4, %2;\n\t"
-      "and.b32 a, a, 4095;\n\t"
-      "or.b32 a, a, %5;\n\t"
-      "ld.shared.u32 w, [a];\n\t"
-      "shr.b32 m, 256, %1;\n\t"
-      "mad.wide.u32 %0, w, m, %0;\n\t"
-      "@p add.s32 %1, %1, -32;\n\t"
-      "popc.b32 n, bal;\n\t"
-      "mad.lo.u32 %2, n, 4, %2;\n\t"
-      "cvt.u32.u64 x, %0;\n\t"
-      "and.b32 t, x, 511;\n\t"
-      "or.b32 t, t, %6;\n\t"
-      "ld.shared.u8 %3, [t];\n\t"
-      "and.b32 len, %3, 15;\n\t"
-      "shr.b64 %0, %0, len;\n\t"
-      "add.s32 %1, %1, len;\n\t"
-      "}"
-      : "+l"(buf), "+r"(nv), "+r"(off), "=r"(ent)
-      : "r"(lt), "r"(base), "r"(lut));
-  return ent;
-}
-
-
-// step_ring with the refill decision of the next symbol taken before this
-// symbol's insert (the one-ahead pipeline of step_piped, ring-addressed): a
-// lane that does not refill here knows this symbol's length from its current
-// buffer, so the next symbol's ballot and word load need not wait for this
-// symbol's insert and lookup.  Both lookups are issued first.  w is the word
-// this lane takes at this symbol if it refills here (loaded one step before).
-__device__ __forceinline__ uint32_t step_ring_piped(uint64_t &buf, int &nv, uint32_t &off,
-                                                    uint32_t &w, uint32_t base, uint32_t lut,
-                                                    uint32_t lenlut, unsigned lt) {
-  uint32_t ent, wn;
-  asm volatile(
-      "{\n\t"
-      ".reg .pred r, pn;\n\t"
-      ".reg .b32 x, ia, la, t, bal, c, a, n, m, ib, len;\n\t"
-      ".reg .b64 bi;\n\t"
-      "setp.ge.s32 r, %1, 0;\n\t"
+      ".reg .pred p0, p1, ev;\n\t"
+      ".reg .b32 x, ia, l0, t, b0, b1, n0, n1, mb, c, a, w, m, len;\n\t"
+      "setp.ge.s32 p0, %1, 0;\n\t"
       "cvt.u32.u64 x, %0;\n\t"
       "and.b32 ia, x, 511;\n\t"
       "or.b32 ia, ia, %8;\n\t"
-      "ld.shared.u8 la, [ia];\n\t"
-      "shr.b32 m, 256, %1;\n\t"
-      "mad.wide.u32 bi, %9, m, %0;\n\t"
-      "cvt.u32.u64 x, bi;\n\t"
-      "and.b32 ib, x, 511;\n\t"
-      "or.b32 ib, ib, %7;\n\t"
-      "ld.shared.u8 %3, [ib];\n\t"
-      "add.s32 t, %1, la;\n\t"
-      "setp.ge.and.s32 pn, t, 0, !r;\n\t"
-      "vote.sync.ballot.b32 bal, pn, 0xffffffff;\n\t"
-      "and.b32 c, bal, %5;\n\t"
-      "popc.b32 c, c;\n\t"
+      "ld.shared.u8 l0, [ia];\n\t"
+      "add.s32 t, %1, l0;\n\t"
+      "setp.ge.and.s32 p1, t, 0, !p0;\n\t"
+      "vote.sync.ballot.b32 b0, p0, 0xffffffff;\n\t"
+      "vote.sync.ballot.b32 b1, p1, 0xffffffff;\n\t"
+      "popc.b32 n0, b0;\n\t"
+      "selp.b32 mb, b0, b1, p0;\n\t"
+      "and.b32 mb, mb, %5;\n\t"
+      "popc.b32 c, mb;\n\t"
+      "@!p0 add.s32 c, c, n0;\n\t"
       "mad.lo.u32 a, c, 4, %2;\n\t"
       "and.b32 a, a, 4095;\n\t"
       "or.b32 a, a, %6;\n\t"
-      "ld.shared.u32 %4, [a];\n\t"
-      "popc.b32 n, bal;\n\t"
-      "mad.lo.u32 %2, n, 4, %2;\n\t"
-      "@r add.s32 %1, %1, -32;\n\t"
+      "ld.shared.u32 w, [a];\n\t"
+      "popc.b32 n1, b1;\n\t"
+      "add.s32 n1, n1, n0;\n\t"
+      "mad.lo.u32 %2, n1, 4, %2;\n\t"
+      "or.pred ev, p0, p1;\n\t"
+      "add.s32 t, %1, 15;\n\t"
+      "shr.b32 m, 8388608, t;\n\t"
+      "@ev mad.wide.u32 %0, w, m, %0;\n\t"
+      "@ev add.s32 %1, %1, -32;\n\t"
+      "cvt.u32.u64 x, %0;\n\t"
+      "and.b32 x, x, 511;\n\t"
+      "or.b32 x, x, %7;\n\t"
+      "ld.shared.u8 %3, [x];\n\t"
       "and.b32 len, %3, 15;\n\t"
-      "shr.b64 %0, bi, len;\n\t"
+      "shr.b64 %0, %0, len;\n\t"
+      "add.s32 %1, %1, len;\n\t"
+      "cvt.u32.u64 x, %0;\n\t"
+      "and.b32 x, x, 511;\n\t"
+      "or.b32 x, x, %7;\n\t"
+      "ld.shared.u8 %4, [x];\n\t"
+      "and.b32 len, %4, 15;\n\t"
+      "shr.b64 %0, %0, len;\n\t"
       "add.s32 %1, %1, len;\n\t"
       "}"
-      : "+l"(buf), "+r"(nv), "+r"(off), "=&r"(ent), "=&r"(wn)
-      : "r"(lt), "r"(base), "r"(lut), "r"(lenlut), "r"(w));
-  w = wn;
-  return ent;
+      : "+l"(buf), "+r"(nv), "+r"(off), "=&r"(e0), "=&r"(e1)
+      : "r"(lt), "r"(base), "r"(lut), "r"(lenlut));
 }
 
 __device__ __forceinline__ void cp_async16_s(uint32_t saddr, const void *gmem) {
@@ -258,11 +234,10 @@ __device__ __forceinline__ void ring_fill(uint32_t base, const uint8_t *src, uin
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
-template <bool kPiped>
 __global__ void __launch_bounds__(kWarps * 32) decode_ring_kernel(const __grid_constant__ DecodeArgs a) {
   extern __shared__ __align__(16) uint8_t s_dyn[];  // kWarps rings of 4 KiB, 4 KiB-aligned
   __shared__ __align__(512) uint8_t s_lut[kWarps][kLutBytes];
-  __shared__ __align__(512) uint8_t s_len[kPiped ? kWarps : 1][kLutBytes];  // lengths only
+  __shared__ __align__(512) uint8_t s_len[kWarps][kLutBytes];  // lengths only
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t j = blockIdx.y;
   const int64_t gg = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
@@ -298,10 +273,9 @@ __global__ void __launch_bounds__(kWarps * 32) decode_ring_kernel(const __grid_c
   w_begin = w_begin < 0 ? 0 : (w_begin > w_end ? w_end : w_begin);
   uint8_t *L = s_lut[warp];
   reinterpret_cast<uint4 *>(L)[lane] = lut_v;
-  if (kPiped)
-    reinterpret_cast<uint4 *>(s_len[warp])[lane] =
-        make_uint4(lut_v.x & 0x0F0F0F0Fu, lut_v.y & 0x0F0F0F0Fu, lut_v.z & 0x0F0F0F0Fu,
-                   lut_v.w & 0x0F0F0F0Fu);
+  reinterpret_cast<uint4 *>(s_len[warp])[lane] =
+      make_uint4(lut_v.x & 0x0F0F0F0Fu, lut_v.y & 0x0F0F0F0Fu, lut_v.z & 0x0F0F0F0Fu,
+                 lut_v.w & 0x0F0F0F0Fu);
   dst_row = dst_row > 0 ? dst_row : 0;
   const uint32_t *nib = reinterpret_cast<const uint32_t *>(rec + head) + g * (chunk / 8) * 32;
   uint8_t *out_row = n.dst + dst_row * n.N + (g * 32 + lane) * chunk;
@@ -330,17 +304,13 @@ __global__ void __launch_bounds__(kWarps * 32) decode_ring_kernel(const __grid_c
   int nv = 8;
   uint32_t off = static_cast<uint32_t>(4 * (a_begin - a0));
   const uint32_t sl = static_cast<uint32_t>(__cvta_generic_to_shared(L));
-  const uint32_t sn = static_cast<uint32_t>(__cvta_generic_to_shared(s_len[kPiped ? warp : 0]));
-  // Pipelined step: every lane refills at symbol 0 (level 0) and takes the
-  // group's first 32 words in lane order.
-  uint32_t w = 0;
-  if (kPiped) {
-    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w) : "r"(base + ((off + 4u * lane) & (kRing - 1))));
-    off += 128;
-  }
-  auto step = [&]() {
-    return kPiped ? step_ring_piped(buf, nv, off, w, base, sl, sn, lt)
-                  : step_ring(buf, nv, off, base, sl, lt);
+  const uint32_t sn = static_cast<uint32_t>(__cvta_generic_to_shared(s_len[warp]));
+  // Four symbols: their LUT entries summed at byte offsets (e0 + e1 << 8 + ...).
+  auto quad = [&]() {
+    uint32_t a0, a1, a2, a3;
+    step_pair(buf, nv, off, base, sl, sn, lt, a0, a1);
+    step_pair(buf, nv, off, base, sl, sn, lt, a2, a3);
+    return mad_u32(a3, 1u << 24, mad_u32(a2, 1u << 16, mad_u32(a1, 1u << 8, a0)));
   };
   const int64_t steps = chunk / 8;
   const int64_t last = steps - 1;
@@ -369,12 +339,8 @@ __global__ void __launch_bounds__(kWarps * 32) decode_ring_kernel(const __grid_c
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const uint32_t nw = h ? q1 : q0;
-      uint32_t acc_lo = step();
-#pragma unroll
-      for (int k = 1; k < 4; ++k) acc_lo = mad_u32(step(), 1u << (8 * k), acc_lo);
-      uint32_t acc_hi = step();
-#pragma unroll
-      for (int k = 1; k < 4; ++k) acc_hi = mad_u32(step(), 1u << (8 * k), acc_hi);
+      const uint32_t acc_lo = quad();
+      const uint32_t acc_hi = quad();
       lohi[2 * h] = merge4(acc_lo, nw & 0xFFFFu);
       lohi[2 * h + 1] = merge4(acc_hi, nw >> 16);
     }
@@ -426,21 +392,7 @@ extern "C" int xp_decode_rows(const int64_t *todo, int64_t K, const int64_t *dst
                    N / (32 * chunk)};
   }
   const int64_t groups = a.n[0].G + a.n[1].G;
-  // Launches of at most 12 warps per SM are latency-bound (three warps or
-  // fewer per scheduler): they take the pipelined step.
-  static std::atomic<int> sm_count[64];
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return XP_EINVAL;
-  int sms = sm_count[dev].load(std::memory_order_relaxed);
-  if (sms == 0) {
-    cudaError_t err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (err != cudaSuccess) return static_cast<int>(err);
-    sms = sms > 0 ? sms : 1;
-    sm_count[dev].store(sms, std::memory_order_relaxed);
-  }
-  const bool piped = K * groups <= int64_t(12) * sms;
   dim3 grid(static_cast<unsigned>((groups + kWarps - 1) / kWarps), static_cast<unsigned>(K));
-  auto kern = piped ? decode_ring_kernel<true> : decode_ring_kernel<false>;
-  kern<<<grid, kWarps * 32, kRingSmem, as_stream(stream)>>>(a);
+  decode_ring_kernel<<<grid, kWarps * 32, kRingSmem, as_stream(stream)>>>(a);
   return launch_status();
 }
