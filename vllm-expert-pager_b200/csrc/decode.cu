@@ -17,12 +17,13 @@
 //    read consecutive words (ballot + popc give each its slot), one
 //    conflict-free shared load.  The ring (instead of staging a whole group,
 //    ~7.3 KiB) lets 10 CTAs share an SM.
-//  * Two symbols per ballot round (step_pair): a lane refills at most once in
-//    two consecutive symbols, its refill time follows from a length-only
-//    lookup of its current buffer, and its word can be inserted above its
-//    valid bits before the first of the two; so one round of two ballots and
-//    one word load serves two symbols, which halves the refill work on the
-//    symbol-to-symbol chain.
+//  * Several symbols per ballot round (step_triple, step_pair; 8 symbols in
+//    rounds of 3 + 3 + 2): a lane refills at most once in three consecutive
+//    symbols, its refill symbol follows from length-only lookups of its current
+//    buffer, and its word can be inserted above its valid bits before the
+//    round's first symbol; so one round of ballots and one word load serves
+//    two or three symbols, which cuts the refill work on the symbol-to-symbol
+//    chain.
 //  * One lookup in the 512-byte LUT per symbol (the table is 512-byte aligned,
 //    so its address is one AND/OR of the window).
 //  * Every instruction is integer work; the integer ALU pipe (one warp
@@ -222,6 +223,89 @@ __device__ __forceinline__ void step_pair(uint64_t &buf, int &nv, uint32_t &off,
       : "r"(lt), "r"(base), "r"(lut), "r"(lenlut));
 }
 
+
+// Three symbols per ballot round: after a refill a lane holds at least 32 bits,
+// so it cannot refill again within the next two symbols; each lane refills at
+// most once in three consecutive symbols.  Its refill symbol k (level < 9 before
+// symbol k, the earlier symbols' lengths from two chained length-only lookups
+// of the current buffer) is known before any of the three is decoded; three
+// ballots order the refills as the format does (symbol i's refilling lanes in
+// lane order, then i+1's, then i+2's) and the word goes in right above the
+// lane's valid bits before symbol i, at most 26 bits up (level < 9 + two codes
+// of at most 9 bits), where the 64-bit buffer holds it; its multiplier
+// 0x4000000 >> (nv + 18) is 1 << level for level <= 26.
+__device__ __forceinline__ void step_triple(uint64_t &buf, int &nv, uint32_t &off, uint32_t base,
+                                            uint32_t lut, uint32_t lenlut, unsigned lt,
+                                            uint32_t &e0, uint32_t &e1, uint32_t &e2) {
+  asm volatile(
+      "{\n\t"
+      ".reg .pred p0, p1, p2, q, ev;\n\t"
+      ".reg .b32 x, lo, hi, l0, l1, t, b0, b1, b2, n0, n1, s01, mb, c, bs, a, w, m, len;\n\t"
+      "setp.ge.s32 p0, %1, 0;\n\t"
+      "mov.b64 {lo, hi}, %0;\n\t"
+      "and.b32 x, lo, 511;\n\t"
+      "or.b32 x, x, %9;\n\t"
+      "ld.shared.u8 l0, [x];\n\t"
+      "shf.r.clamp.b32 x, lo, hi, l0;\n\t"
+      "and.b32 x, x, 511;\n\t"
+      "or.b32 x, x, %9;\n\t"
+      "ld.shared.u8 l1, [x];\n\t"
+      "add.s32 t, %1, l0;\n\t"
+      "setp.ge.and.s32 p1, t, 0, !p0;\n\t"
+      "or.pred q, p0, p1;\n\t"
+      "add.s32 t, t, l1;\n\t"
+      "setp.ge.and.s32 p2, t, 0, !q;\n\t"
+      "vote.sync.ballot.b32 b0, p0, 0xffffffff;\n\t"
+      "vote.sync.ballot.b32 b1, p1, 0xffffffff;\n\t"
+      "vote.sync.ballot.b32 b2, p2, 0xffffffff;\n\t"
+      "popc.b32 n0, b0;\n\t"
+      "popc.b32 n1, b1;\n\t"
+      "add.s32 s01, n0, n1;\n\t"
+      "selp.b32 mb, b1, b2, p1;\n\t"
+      "selp.b32 mb, b0, mb, p0;\n\t"
+      "selp.b32 bs, n0, s01, p1;\n\t"
+      "selp.b32 bs, 0, bs, p0;\n\t"
+      "and.b32 mb, mb, %6;\n\t"
+      "popc.b32 c, mb;\n\t"
+      "add.s32 c, c, bs;\n\t"
+      "mad.lo.u32 a, c, 4, %2;\n\t"
+      "and.b32 a, a, 4095;\n\t"
+      "or.b32 a, a, %7;\n\t"
+      "ld.shared.u32 w, [a];\n\t"
+      "popc.b32 n1, b2;\n\t"
+      "add.s32 n1, n1, s01;\n\t"
+      "mad.lo.u32 %2, n1, 4, %2;\n\t"
+      "or.pred ev, q, p2;\n\t"
+      "add.s32 t, %1, 18;\n\t"
+      "shr.b32 m, 67108864, t;\n\t"
+      "@ev mad.wide.u32 %0, w, m, %0;\n\t"
+      "@ev add.s32 %1, %1, -32;\n\t"
+      "cvt.u32.u64 x, %0;\n\t"
+      "and.b32 x, x, 511;\n\t"
+      "or.b32 x, x, %8;\n\t"
+      "ld.shared.u8 %3, [x];\n\t"
+      "and.b32 len, %3, 15;\n\t"
+      "shr.b64 %0, %0, len;\n\t"
+      "add.s32 %1, %1, len;\n\t"
+      "cvt.u32.u64 x, %0;\n\t"
+      "and.b32 x, x, 511;\n\t"
+      "or.b32 x, x, %8;\n\t"
+      "ld.shared.u8 %4, [x];\n\t"
+      "and.b32 len, %4, 15;\n\t"
+      "shr.b64 %0, %0, len;\n\t"
+      "add.s32 %1, %1, len;\n\t"
+      "cvt.u32.u64 x, %0;\n\t"
+      "and.b32 x, x, 511;\n\t"
+      "or.b32 x, x, %8;\n\t"
+      "ld.shared.u8 %5, [x];\n\t"
+      "and.b32 len, %5, 15;\n\t"
+      "shr.b64 %0, %0, len;\n\t"
+      "add.s32 %1, %1, len;\n\t"
+      "}"
+      : "+l"(buf), "+r"(nv), "+r"(off), "=&r"(e0), "=&r"(e1), "=&r"(e2)
+      : "r"(lt), "r"(base), "r"(lut), "r"(lenlut));
+}
+
 __device__ __forceinline__ void cp_async16_s(uint32_t saddr, const void *gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(gmem) : "memory");
 }
@@ -305,12 +389,15 @@ __global__ void __launch_bounds__(kWarps * 32) decode_ring_kernel(const __grid_c
   uint32_t off = static_cast<uint32_t>(4 * (a_begin - a0));
   const uint32_t sl = static_cast<uint32_t>(__cvta_generic_to_shared(L));
   const uint32_t sn = static_cast<uint32_t>(__cvta_generic_to_shared(s_len[warp]));
-  // Four symbols: their LUT entries summed at byte offsets (e0 + e1 << 8 + ...).
-  auto quad = [&]() {
-    uint32_t a0, a1, a2, a3;
-    step_pair(buf, nv, off, base, sl, sn, lt, a0, a1);
-    step_pair(buf, nv, off, base, sl, sn, lt, a2, a3);
-    return mad_u32(a3, 1u << 24, mad_u32(a2, 1u << 16, mad_u32(a1, 1u << 8, a0)));
+  // Eight symbols in rounds of 3 + 3 + 2: their LUT entries summed at byte
+  // offsets, symbols 0-3 into lo and 4-7 into hi.
+  auto octet = [&](uint32_t &lo, uint32_t &hi) {
+    uint32_t e[8];
+    step_triple(buf, nv, off, base, sl, sn, lt, e[0], e[1], e[2]);
+    step_triple(buf, nv, off, base, sl, sn, lt, e[3], e[4], e[5]);
+    step_pair(buf, nv, off, base, sl, sn, lt, e[6], e[7]);
+    lo = mad_u32(e[3], 1u << 24, mad_u32(e[2], 1u << 16, mad_u32(e[1], 1u << 8, e[0])));
+    hi = mad_u32(e[7], 1u << 24, mad_u32(e[6], 1u << 16, mad_u32(e[5], 1u << 8, e[4])));
   };
   const int64_t steps = chunk / 8;
   const int64_t last = steps - 1;
@@ -339,8 +426,8 @@ __global__ void __launch_bounds__(kWarps * 32) decode_ring_kernel(const __grid_c
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const uint32_t nw = h ? q1 : q0;
-      const uint32_t acc_lo = quad();
-      const uint32_t acc_hi = quad();
+      uint32_t acc_lo, acc_hi;
+      octet(acc_lo, acc_hi);
       lohi[2 * h] = merge4(acc_lo, nw & 0xFFFFu);
       lohi[2 * h + 1] = merge4(acc_hi, nw >> 16);
     }
