@@ -12,11 +12,11 @@
 // = (s & 8) << 4 | sym << 3 | (s & 7) with s the stored sign/mantissa nibble.
 //
 // B200 mapping: one warp per group, four groups per CTA.
-//  * The group's Huffman words stream through a 4 KiB shared-memory ring per
+//  * The group's Huffman words stream through a 2 KiB shared-memory ring per
 //    warp, filled by cp.async half a ring ahead of the reader; refilling lanes
 //    read consecutive words (ballot + popc give each its slot), one
 //    conflict-free shared load.  The ring (instead of staging a whole group,
-//    ~7.3 KiB) lets 10 CTAs share an SM.
+//    ~7.3 KiB) and a 48-register bound let 10 CTAs (40 warps) share an SM.
 //  * Several symbols per ballot round (step_triple, step_pair; 8 symbols in
 //    rounds of 3 + 3 + 2): a lane refills at most once in three consecutive
 //    symbols, its refill symbol follows from length-only lookups of its current
@@ -145,17 +145,23 @@ __device__ __forceinline__ uint32_t merge4(uint32_t acc, uint32_t x) {
   return bitsel(acc >> 1, mul_u32(t, 17u), 0x78787878u);
 }
 
-// Word ring.  Each warp streams its group's Huffman words through a 4 KiB
-// shared-memory ring (1,024 words), filled half by half (2 KiB = 128 cp.async
-// units of 16 bytes, 4 per lane) as the read offset enters the newest half;
-// a half in flight is waited for only when the reader comes within 1 KiB of
-// it.  A valid record's refills advance the reader by at most 6 words per lane
-// per 16 symbols (a lane refills at most once every 3 symbols), 768 bytes, so
-// a fill issued half a ring ahead has about 70 symbol steps to land.  Word
-// addresses are (offset & 4095) | base with a 4 KiB-aligned base, so no read
-// leaves the ring whatever the record holds: a corrupt record can only decode
-// to wrong bytes.
-constexpr uint32_t kRing = 4096, kHalf = 2048;
+// Word ring.  Each warp streams its group's Huffman words through a 2 KiB
+// shared-memory ring (512 words), filled half by half (1 KiB = 64 cp.async
+// units of 16 bytes, 2 per lane) as the read offset enters the newest half.
+// A valid record's refills advance the reader by at most 6 words per lane per
+// 16 symbols (a lane refills at most once every 3 symbols), kMaxAdvance = 768
+// bytes, the only words whose values matter (lanes that do not refill read
+// words they discard); so a half in flight is waited for, at the top of a
+// 16-symbol iteration, only when the reader is within 768 bytes of it, which
+// leaves a fill 256 bytes (~18 symbol steps) to land.  Word addresses are
+// (offset & 2047) | base with a 2 KiB-aligned base, so no read leaves the ring
+// whatever the record holds: a corrupt record can only decode to wrong bytes.
+constexpr uint32_t kRing = 2048, kHalf = 1024;
+#define XP_RING_MASK "2047"  // kRing - 1, spelled for the step functions' PTX
+static_assert(kRing == 2048, "XP_RING_MASK spells kRing - 1");
+// Most stream bytes a valid record's refills consume in 16 symbols: a lane
+// refills at most once every 3 symbols, so 6 words per lane.
+constexpr uint32_t kMaxAdvance = 6 * 32 * 4;
 // Dynamic shared memory per CTA: kWarps rings plus the slack that aligns them.
 constexpr size_t kRingSmem = kWarps * kRing + kRing;
 
@@ -193,7 +199,7 @@ __device__ __forceinline__ void step_pair(uint64_t &buf, int &nv, uint32_t &off,
       "popc.b32 c, mb;\n\t"
       "@!p0 add.s32 c, c, n0;\n\t"
       "mad.lo.u32 a, c, 4, %2;\n\t"
-      "and.b32 a, a, 4095;\n\t"
+      "and.b32 a, a, " XP_RING_MASK ";\n\t"
       "or.b32 a, a, %6;\n\t"
       "ld.shared.u32 w, [a];\n\t"
       "popc.b32 n1, b1;\n\t"
@@ -269,7 +275,7 @@ __device__ __forceinline__ void step_triple(uint64_t &buf, int &nv, uint32_t &of
       "popc.b32 c, mb;\n\t"
       "add.s32 c, c, bs;\n\t"
       "mad.lo.u32 a, c, 4, %2;\n\t"
-      "and.b32 a, a, 4095;\n\t"
+      "and.b32 a, a, " XP_RING_MASK ";\n\t"
       "or.b32 a, a, %7;\n\t"
       "ld.shared.u32 w, [a];\n\t"
       "popc.b32 n1, b2;\n\t"
@@ -318,8 +324,8 @@ __device__ __forceinline__ void ring_fill(uint32_t base, const uint8_t *src, uin
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
-__global__ void __launch_bounds__(kWarps * 32) decode_ring_kernel(const __grid_constant__ DecodeArgs a) {
-  extern __shared__ __align__(16) uint8_t s_dyn[];  // kWarps rings of 4 KiB, 4 KiB-aligned
+__global__ void __launch_bounds__(kWarps * 32, 10) decode_ring_kernel(const __grid_constant__ DecodeArgs a) {
+  extern __shared__ __align__(16) uint8_t s_dyn[];  // kWarps rings of 2 KiB, 2 KiB-aligned
   __shared__ __align__(512) uint8_t s_lut[kWarps][kLutBytes];
   __shared__ __align__(512) uint8_t s_len[kWarps][kLutBytes];  // lengths only
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -417,7 +423,7 @@ __global__ void __launch_bounds__(kWarps * 32) decode_ring_kernel(const __grid_c
       filled = hi;
       pending = true;
     }
-    if (pending && off + 1024 + kHalf >= filled) {
+    if (pending && off + kMaxAdvance + kHalf >= filled) {
       asm volatile("cp.async.wait_group 0;" ::: "memory");
       __syncwarp();
       pending = false;
