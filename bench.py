@@ -930,7 +930,8 @@ def run_reference_triton(args) -> None:
       first gather runs without ``fetch=``: with every expert in RAM the SSD list is
       empty and ``fetch=`` only adds a program that publishes nothing;
     * ``decode_k8`` / ``decode_k64``: ``decode_rows`` on config-1 records made by the
-      reference's ``codec.encode`` (pitch 0.89), as ``bench_decode``.
+      reference's ``codec.encode`` (pitch 0.89), timed from a CUDA graph as
+      ``bench_decode``.
     """
     line = {"impl": "reference", "workload": "reference-triton"}
     if not os.path.isdir(os.path.join(REF_DIR, "vllm_expert_pager")):
@@ -1069,25 +1070,37 @@ def run_reference_triton(args) -> None:
         starts = list(range(0, distinct - K + 1, K))
         todos = [torch.arange(s0, s0 + K, dtype=torch.int64, device=device) for s0 in starts]
 
+        views = [[x[s0 : s0 + K] for x in stg] for s0 in starts]
+
         def launch(i):
-            s0 = starts[i % len(starts)]
-            rcodec.decode_rows(todos[i % len(starts)], ident, no_cache,
-                               [x[s0 : s0 + K] for x in stg], dst, lut)
+            j = i % len(starts)
+            rcodec.decode_rows(todos[j], ident, no_cache, views[j], dst, lut)
 
         for i in range(4):
             launch(i)
         torch.cuda.synchronize()
+        # Timed as bench_decode times this library's decoder: 48 launches captured in
+        # a CUDA graph (the reference captures its decode path in graphs too), the
+        # replay bracketed by events on its stream, best of 5.
+        s = torch.cuda.Stream(device=device)
+        s.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(s):
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=s):
+                for i in range(48):
+                    launch(i)
+        torch.cuda.synchronize()
         best = None
-        for _ in range(3):
-            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                  for _ in range(24)]
-            for i in range(24):
-                ev[i][0].record()
-                launch(i)
-                ev[i][1].record()
+        for _ in range(5):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(s):
+                a.record()
+                graph.replay()
+                b.record()
             torch.cuda.synchronize()
-            t = sum(a.elapsed_time(b) for a, b in ev) * 1e3 / 24
+            t = a.elapsed_time(b) * 1e3 / 48
             best = t if best is None else min(best, t)
+        del graph
         for n, d in zip(names, dst):
             if not torch.equal(d[K - 1].cpu(), raws[n][(K - 1) % 8]):
                 raise SystemExit(f"reference decode mismatch ({n})")
