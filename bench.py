@@ -331,7 +331,9 @@ def bench_decode(device, rows_per_launch: int, launches: int = 48, distinct: int
     return {"rows_per_launch": K, "us_per_launch": round(best, 2),
             "algorithmic_bytes_per_launch": int(K * per_row), "achieved": round(achieved, 1),
             "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "bound": "hbm",
-            "peak_source": src}
+            "peak_source": src,
+            "how": f"{launches} launches captured in a CUDA graph, replay timed with CUDA events "
+                   f"on its stream, best of {reps}"}
 
 
 class PagedMoE:
@@ -1107,7 +1109,9 @@ def run_reference_triton(args) -> None:
         achieved = K * per_row / (best * 1e-6) / 1e9
         kernels[f"decode_k{K}"] = {"rows_per_launch": K, "us_per_launch": round(best, 2),
                                    "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                                   "frac": round(achieved / peak, 4), "peak_source": psrc}
+                                   "frac": round(achieved / peak, 4), "peak_source": psrc,
+                                   "how": "48 launches captured in a CUDA graph, replay timed "
+                                          "with CUDA events on its stream, best of 5"}
     kernels["plan_config5"] = time_planning(ExpertTable, syn, device)
     line["kernels"] = kernels
     line["device"] = torch.cuda.get_device_name(device)
