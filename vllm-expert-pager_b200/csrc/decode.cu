@@ -341,9 +341,9 @@ __global__ void __launch_bounds__(kWarps * 32, 10) decode_ring_kernel(const __gr
   const int32_t *hdr = reinterpret_cast<const int32_t *>(rec);
   const int64_t huff_w = (head + n.N / 2) / 4;
   const int64_t rec_w = n.P / 4;
-  // Three global round trips: the todo entry and the
-  // group's word range; the skip list, cache/destination rows and LUT; then
-  // the group's first ring of words.
+  // Three global round trips: the todo entry and the group's word range; the
+  // skip list, cache/destination rows and LUT; then the group's first ring of
+  // words.
   const int64_t e = a.todo[j];
   int64_t w_begin = hdr[g], w_end = hdr[g + 1];
   if (e < 0) return;
@@ -391,7 +391,7 @@ __global__ void __launch_bounds__(kWarps * 32, 10) decode_ring_kernel(const __gr
 
   const unsigned lt = lanemask_lt();
   uint64_t buf = 0;
-  int nv = 8;
+  int nv = 8;  // 8 - level: level < 9 (a refill) iff nv >= 0
   uint32_t off = static_cast<uint32_t>(4 * (a_begin - a0));
   const uint32_t sl = static_cast<uint32_t>(__cvta_generic_to_shared(L));
   const uint32_t sn = static_cast<uint32_t>(__cvta_generic_to_shared(s_len[warp]));
