@@ -36,6 +36,12 @@ extern "C" {
 /* Limits of the table kernels: E <= XP_MAX_EXPERTS, S <= XP_MAX_SLOTS. */
 #define XP_MAX_EXPERTS 4096
 #define XP_MAX_SLOTS 2048
+/* Limits of the gather / fetch arguments (larger values are XP_EINVAL): copying
+ * CTAs (ctas), the re-publish interval of an SSD wait (retry_ns, at most one
+ * hour) and the number of re-publishes before it gives up (giveup). */
+#define XP_MAX_COPY_CTAS 1024
+#define XP_MAX_RETRY_NS 3600000000000LL
+#define XP_MAX_GIVEUP (1 << 20)
 
 /* Library version, and a static description of a status code. */
 int xp_version(void);

@@ -51,6 +51,19 @@ def test_device_calls_reject_bad_arguments_before_launching():
     assert lib.xp_fetch_wait(None, 1, None, None, None, 256, 4, 1, 1, None) == native.XP_EINVAL
 
 
+def test_fetch_wait_limits_are_checked_before_launching():
+    # A wait interval above one hour or more than 2**20 re-publishes is refused, so the
+    # device-side time limit (giveup + 2) * retry_ns cannot overflow.
+    lib = native.lib()
+    buf = (ctypes.c_int64 * 64)()
+    p = ctypes.addressof(buf)
+    one_hour = 3600 * 10**9
+    assert lib.xp_fetch_wait(p, 1, p, p, p, 8, 4, one_hour + 1, 1, None) == native.XP_EINVAL
+    assert lib.xp_fetch_wait(p, 1, p, p, p, 8, 4, 1, (1 << 20) + 1, None) == native.XP_EINVAL
+    assert lib.xp_fetch(p, 1, p, 0, 0, p, p, p, 8, 4, one_hour + 1, 1, None) == native.XP_EINVAL
+    assert lib.xp_fetch(p, 1, p, 0, 0, p, p, p, 8, 4, 1, -1, None) == native.XP_EINVAL
+
+
 def test_encode_scratch_size_and_argument_checks():
     lib = native.lib()
     # 2 MiB rows, chunk 512: G = 128 groups -> 256-byte-rounded per-row scratch.

@@ -112,10 +112,12 @@ extern "C" int xp_gather_rows(const int64_t *todo, int64_t K, const int64_t *dst
   bool vec;
   if (!fill_names(a.job, srcs, caches, dsts, stgs, Ws, Ps, scales, sdsts, SWs, compress, vec))
     return XP_EINVAL;
+  if (ctas < 0 || ctas > XP_MAX_COPY_CTAS) return XP_EINVAL;
   a.copy_ctas = ctas > 0 ? ctas : kDefaultCtas;
   a.fetch = req != nullptr;
   if (a.fetch) {
-    if (!skip || !ring_ok(seq, req, done, block, ring) || K > block || retry_ns < 0 || giveup < 0)
+    if (!skip || !ring_ok(seq, req, done, block, ring) || K > block || retry_ns < 0 ||
+        retry_ns > XP_MAX_RETRY_NS || giveup < 0 || giveup > XP_MAX_GIVEUP)
       return XP_EINVAL;
     a.f = Fetch{skip, K, src_row, base, layer, seq, seq, req, done, block, ring, retry_ns, giveup};
   }
@@ -143,7 +145,7 @@ extern "C" int xp_fetch_wait(const int64_t *todo, int64_t K, const int64_t *tick
                              const int64_t *done, int64_t block, int64_t ring, int64_t retry_ns,
                              int64_t giveup, void *stream) {
   if (K < 0 || (K > 0 && !todo) || !ticket || !req || !done || block < 1 || ring < 1 ||
-      retry_ns < 0 || giveup < 0)
+      retry_ns < 0 || retry_ns > XP_MAX_RETRY_NS || giveup < 0 || giveup > XP_MAX_GIVEUP)
     return XP_EINVAL;
   Fetch f{todo, K, nullptr, 0, 0, nullptr, const_cast<int64_t *>(ticket), req, done, block, ring,
           retry_ns, giveup};
@@ -156,7 +158,7 @@ extern "C" int xp_fetch(const int64_t *todo, int64_t K, const int64_t *row_of, i
                         int64_t block, int64_t ring, int64_t retry_ns, int64_t giveup,
                         void *stream) {
   if (K < 0 || (K > 0 && (!todo || !row_of)) || K > block || !ring_ok(seq, req, done, block, ring) ||
-      retry_ns < 0 || giveup < 0)
+      retry_ns < 0 || retry_ns > XP_MAX_RETRY_NS || giveup < 0 || giveup > XP_MAX_GIVEUP)
     return XP_EINVAL;
   // gather.py:285-287: the ticket is seq itself.
   Fetch f{todo, K, row_of, base, layer, seq, seq, req, done, block, ring, retry_ns, giveup};

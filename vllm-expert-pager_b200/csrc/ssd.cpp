@@ -355,6 +355,7 @@ extern "C" const char *ssd_error(void *server) {
 }
 
 extern "C" void ssd_set_read_chunk(void *server, long bytes) {
+  if (!server) return;
   static_cast<Server *>(server)->read_chunk.store(bytes < 0 ? 0 : bytes, std::memory_order_relaxed);
 }
 

@@ -175,7 +175,7 @@ extern "C" int xp_decode_step(
     if (!t->slot_of || !t->expert_in || !t->last_used || !t->counters || t->slots < 1 ||
         t->slots > XP_MAX_SLOTS || K > t->slots)
       return XP_EINVAL;
-  if (K > gdev::kMaxK) return XP_EINVAL;
+  if (K > gdev::kMaxK || ctas < 0 || ctas > XP_MAX_COPY_CTAS) return XP_EINVAL;
   const void *srcs[2] = {src0, src1}, *caches[2] = {dst0, dst1};
   void *dsts[2] = {dst0, dst1}, *stgs[2] = {stg0, stg1};
   const void *scales[2] = {scale0, scale1};
@@ -186,7 +186,7 @@ extern "C" int xp_decode_step(
     return XP_EINVAL;
   p.fetch = req != nullptr;
   if (p.fetch && (!seq || !done || block < 1 || ring < 1 || K > block || retry_ns < 0 ||
-                  giveup < 0))
+                  retry_ns > XP_MAX_RETRY_NS || giveup < 0 || giveup > XP_MAX_GIVEUP))
     return XP_EINVAL;
   // Pass 1: the VRAM misses that are in RAM (the SSD misses are skipped).
   p.ram.todo = a_todo;
