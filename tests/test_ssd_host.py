@@ -230,6 +230,30 @@ def test_random_sequence_matches_reference_server(tmp_path):
             ring.close()
 
 
+@pytest.mark.skipif(not os.path.exists(REF), reason="reference server not built")
+def test_chunked_reads_match_the_reference_server(tmp_path):
+    """This server splitting every record into page-sized jobs, against the reference's
+    server reading whole records: 40 random requests leave identical RAM tiers and stats."""
+    rng = np.random.default_rng(11)
+    rings = [Ring(load_server(p), tmp_path, 3, 24, 8) for p in (None, REF)]
+    try:
+        rings[0].so.ssd_set_read_chunk(ctypes.c_void_p(rings[0].h), 4096)
+        for _ in range(40):
+            layer = int(rng.integers(0, 3))
+            n = int(rng.integers(1, 9))
+            experts = rng.choice(24, n, replace=False).tolist()
+            rows = rng.choice(3 * 8 + 2, n, replace=False).tolist()
+            for ring in rings:
+                ring.wait(ring.publish(layer, experts, rows))
+        a, b = rings
+        for k in range(2):
+            assert np.array_equal(a.pinned[k], b.pinned[k])
+        assert a.stats() == b.stats() and a.error() == b.error() is None
+    finally:
+        for ring in rings:
+            ring.close()
+
+
 def test_threads_bound_to_the_ram_tier_node(tmp_path):
     """The server runs on the CPUs of the NUMA node holding the RAM tier (or stays
     unbound when the kernel reports no node), and still serves requests."""
