@@ -6,12 +6,13 @@ vLLM: ``experts.py`` of this package owns a ``LayerPager`` per MoE layer and
 only adds the vLLM hooks around it, and the benchmark drives it directly.
 
 * Decode (``topk_ids.numel() <= cache_slots``, experts.py:380-453): one
-  acquire launch updates the VRAM and RAM tables; one gather launch copies the
+  ``xp_decode_step`` launch updates the VRAM and RAM tables, copies the
   RAM-resident misses (pinned host memory -> slab, or -> staging when
-  compressed) while its last CTA asks the host for the SSD misses and waits;
-  a decode launch expands the staged rows; a second gather (+ decode) copies the
-  rows the host just read.  The MoE then runs on the cache slab with
-  ``expert_map``.
+  compressed) while a CTA asks the host for the SSD misses and waits, then
+  copies the rows the host read; one decode launch expands the staged rows when
+  compressed.  (``fused=False`` runs the reference's sequence instead: acquire,
+  gather + fetch, decode, gather, decode.)  The MoE then runs on the cache slab
+  with ``expert_map``.
 * Working (``numel() > cache_slots``, experts.py:455-577): the RAM table
   acquires or is seeded, ``plan_chunks`` lays the needed experts out in N
   chunks of W rows, and each chunk is copied into a working slab and run
