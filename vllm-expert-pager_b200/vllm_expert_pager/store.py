@@ -11,7 +11,10 @@ request ring and statistics.  What changed:
   CUDA tensor over the same bytes (the reference used vLLM's
   ``get_accelerator_view_from_cpu_tensor``).
 * The host server is the C++ one in ``libxpager.so`` (same C ABI as the
-  reference's C server: ssd_start/ssd_stop/ssd_stats/ssd_error/ssd_test_delay).
+  reference's C server: ssd_start/ssd_stop/ssd_stats/ssd_error/ssd_test_delay),
+  which also splits each record read into page-aligned jobs read by all its
+  threads at once (``VLLM_EXPERT_PAGER_READ_CHUNK``, 512 KiB; 0 reads whole
+  records as the reference does).
 * The GPU's wait for the host is bounded by time: ``retry_ns`` between
   re-publishes and ``giveup`` re-publishes (settable per store).
 
