@@ -171,6 +171,15 @@ int xp_fetch(const int64_t *todo, int64_t K, const int64_t *row_of, int64_t base
  * every launch leaves it zeroed again except the error counter, word 3). */
 #define XP_STEP_SCRATCH_BYTES 16
 
+/* No counterpart in the reference.  Limits, in nanoseconds, of the fused
+ * step's waits on its own CTAs: table_ns for the table updates (default 2 s),
+ * ssd_ns for the SSD fetch CTA (default (giveup + 2) * retry_ns + 2 s, longer
+ * than the fetch CTA's own bounded wait).  A negative value restores the
+ * default; values above XP_MAX_RETRY_NS are XP_EINVAL.  Process-wide, read at
+ * each launch.  A wait that runs out is counted as a give-up (see
+ * xp_decode_step); tests use short limits to make one run out. */
+int xp_set_step_wait_ns(int64_t table_ns, int64_t ssd_ns);
+
 /* Replaces the decode path's three launches (experts.py:406-447: AcquirePair,
  * gather_rows with fetch, gather_rows of the SSD misses) with one: CTA 0/1
  * update the VRAM table a and the RAM table b exactly as xp_acquire_pair
@@ -183,11 +192,17 @@ int xp_fetch(const int64_t *todo, int64_t K, const int64_t *row_of, int64_t base
  * no_cache, ...) without skip.  no_cache: int64[E] of -1.  scratch:
  * XP_STEP_SCRATCH_BYTES of device memory, 16-byte aligned, zeroed before the
  * first call and not shared by launches that may overlap; scratch word 3
- * (uint32) counts waits that gave up.  topk_ids may be pinned host memory
- * (read through the host link).  expert_map_host (may be NULL; no counterpart
- * in the reference) is device-mapped pinned host memory that receives a copy
- * of expert_map[E] from the kernel, so that a host-driven caller needs no
- * copy-engine transfer per step. */
+ * (uint32) counts waits that gave up (the rows of that step are then stale).
+ * errors_out (may be NULL; no counterpart in the reference): device memory or
+ * device-mapped pinned host memory into which a wait that gives up stores the
+ * new count, so that the host can watch for give-ups without a
+ * synchronisation.  topk_ids may be pinned host memory (read through the host
+ * link).  expert_map_host (may be NULL; no counterpart in the reference) is
+ * device-mapped pinned host memory that receives a copy of expert_map[E] from
+ * the kernel, so that a host-driven caller needs no copy-engine transfer per
+ * step.  The copy CTAs wait for the others, so the launch is refused with
+ * XP_ERANGE when its 2 + ctas (+1 with req) CTAs cannot all be resident on the
+ * device at once. */
 int xp_decode_step(const void *topk_ids, int ids_bytes, int64_t K, int64_t E,
                    int64_t *a_slot_of, int64_t *a_expert_in, int64_t *a_last_used,
                    int64_t *a_counters, int64_t a_slots, int32_t *expert_map,
@@ -201,7 +216,7 @@ int xp_decode_step(const void *topk_ids, int ids_bytes, int64_t K, int64_t E,
                    const void *scale1, void *sdst1, int64_t SW1,
                    int compress, int ctas, int64_t layer, int64_t *seq, int64_t *req,
                    const int64_t *done, int64_t block, int64_t ring, int64_t retry_ns,
-                   int64_t giveup, uint32_t *scratch, void *stream);
+                   int64_t giveup, uint32_t *scratch, uint32_t *errors_out, void *stream);
 
 /* Size of the device array xp_decode_step_noalloc takes its scratch from. */
 #define XP_NOALLOC_SCRATCH_BYTES (32u << 20)
@@ -213,10 +228,15 @@ int xp_decode_step(const void *topk_ids, int ids_bytes, int64_t K, int64_t E,
  * lut, chunk), with the flag block and the staging rows taken from a fixed
  * XP_NOALLOC_SCRATCH_BYTES array compiled into the library, held by every GPU
  * that loads it.  Row sizes W/P are in 32-bit words as in xp_decode_step.
- * Returns XP_ERANGE (nothing launched) if 256 + K*(P0+P1)*4 staging bytes do
- * not fit the array.  The first call on a device looks the array up and
- * clears its flags (synchronous): make it before any stream capture.  All
- * calls on a device share the array; calls that overlap on the GPU race. */
+ * Returns XP_ERANGE (nothing launched) if K > 2048 or if 256 + K*(P0+P1)*4
+ * staging bytes do not fit the array.  The first call on a device looks the
+ * array up (which may load the library's device code: make that call before
+ * any stream capture) and queues a clear of its flags on `stream`; the address
+ * is kept for the life of the device's primary context, so do not call this
+ * again after cudaDeviceReset.  All calls on a device share the array; calls
+ * that overlap on the GPU race.  errors_out (may be NULL) receives the running
+ * count of the step's waits that gave up, as in xp_decode_step: the array's
+ * own counter is not reachable from the host. */
 int xp_decode_step_noalloc(const void *topk_ids, int ids_bytes, int64_t K, int64_t E,
                            int64_t *a_slot_of, int64_t *a_expert_in, int64_t *a_last_used,
                            int64_t *a_counters, int64_t a_slots, int32_t *expert_map,
@@ -231,7 +251,7 @@ int xp_decode_step_noalloc(const void *topk_ids, int ids_bytes, int64_t K, int64
                            int compress, const uint8_t *lut, int64_t chunk, int ctas,
                            int64_t layer, int64_t *seq, int64_t *req, const int64_t *done,
                            int64_t block, int64_t ring, int64_t retry_ns, int64_t giveup,
-                           void *stream);
+                           uint32_t *errors_out, void *stream);
 
 /* ---- decode (subsystem 3) ---- */
 

@@ -3,11 +3,11 @@
 The reference (monochromegane/vllm-expert-pager) keeps its C server as a string
 (``_C_SOURCE`` in src/vllm_expert_pager/store.py) and compiles it at first use
 with ``cc -O3 -march=native -funroll-loops -fPIC -shared -pthread``
-(native.py:25).  This script reads that string from a reference checkout,
+(native.py:25).  This script reads that string from the reference's store.py,
 writes it to a temporary directory outside the repository and compiles it the
 same way; only the shared library lands in ``oracle/_ref/`` (git-ignored).
 
-Usage: python oracle/build_ref.py <reference checkout>
+Usage: python oracle/build_ref.py <reference checkout or install directory>
 Tests load the library, when present, to compare the reference server with
 this repository's C++ server on the same request sequences.
 """
@@ -22,7 +22,11 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 
 def source_of(reference: str) -> str:
+    """``_C_SOURCE`` of the reference's store.py, from a checkout (``src/...``)
+    or from an installed copy of the package (``pip install --target``)."""
     path = os.path.join(reference, "src", "vllm_expert_pager", "store.py")
+    if not os.path.exists(path):
+        path = os.path.join(reference, "vllm_expert_pager", "store.py")
     tree = ast.parse(open(path).read())
     for node in tree.body:
         if isinstance(node, ast.Assign) and any(

@@ -76,3 +76,31 @@ def test_encode_scratch_size_and_argument_checks():
                               None) == native.XP_EINVAL
     assert lib.xp_encode_rows(None, 0, 4096, 8192, 64, None, None, None, None, 0,
                               None) == native.XP_OK
+
+
+def test_step_wait_limits_are_checked():
+    lib = native.lib()
+    one_hour = 3600 * 10**9
+    assert lib.xp_set_step_wait_ns(one_hour + 1, -1) == native.XP_EINVAL
+    assert lib.xp_set_step_wait_ns(-1, one_hour + 1) == native.XP_EINVAL
+    assert lib.xp_set_step_wait_ns(-1, -1) == native.XP_OK
+
+
+def test_noalloc_sizes_are_bounded_before_multiplying():
+    # K above the step's list limit, or a pitch beyond the array, is XP_ERANGE before
+    # K x (P0 + P1) x 4 is formed: 8 x 2**60 words would wrap to a small size.
+    lib = native.lib()
+    table_a = [None] * 4 + [8] + [None] * 3
+    table_b = [None] * 4 + [16] + [None] * 2
+
+    def call(K, P0, P1):
+        return lib.xp_decode_step_noalloc(
+            None, 4, K, 32, *table_a, *table_b, None, 0,
+            None, None, 16, P0, None, None, 16, P1,
+            None, None, 4, None, None, 4,
+            1, None, 512, 16, 0, None, None, None, 256, 4, 1, 1, None, None)
+
+    assert call(8, 1 << 60, 16) == native.XP_ERANGE
+    assert call(8, 16, 1 << 60) == native.XP_ERANGE
+    assert call(2049, 16, 16) == native.XP_ERANGE
+    assert call(4, 1 << 22, 1 << 22) == native.XP_ERANGE  # 4 x 32 MiB: beyond the array

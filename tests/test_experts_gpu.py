@@ -88,8 +88,67 @@ def test_hook_outputs_match_unpaged_moe(experts_mod):
             torch.cuda.synchronize()
             assert torch.equal(out, ref), f"step {step} layer {layer}"
     assert ex._store.failed is None and ex._store.reads > 0
+    assert all(m._expert_pager.step_errors() == 0 for m in layers)
     # Parameters are back to their one-row placeholders after every forward.
     assert layers[0].w13_weight.shape[0] == 1 and layers[0].expert_map is None
+    # A decode-step wait that gave up (planted in the pinned host copy the kernel
+    # keeps) stops the next eager forward, as a failed SSD read does.
+    layers[1]._expert_pager.step_errors_host[0] = 2
+    with pytest.raises(RuntimeError, match="gave up"):
+        layers[1].forward_modular(x, tw, ids)
+    layers[1]._expert_pager.step_errors_host[0] = 0
+
+
+def test_hook_replays_in_a_cuda_graph(experts_mod):
+    """forward_modular of a batch-1 decode step, captured once in a CUDA graph with no
+    host synchronisation inside the capture, then replayed with new x / topk_ids /
+    topk_weights written into the captured buffers: every replay equals the eager
+    unpaged MoE bit for bit (compressed RAM tier + SSD tier, both layers)."""
+    from vllm_expert_pager import moe, synthetic
+
+    ex = experts_mod
+    weights = [synthetic.fp8_experts_device(E, DEV, seed=40 + layer) for layer in range(L)]
+    config = moe.moe_config((E, 2 * I, H), (E, H, I), TOPK, 64)
+    layers = make_layers(ex, weights, config)
+    g = torch.Generator(device=DEV).manual_seed(3)
+
+    def draw():
+        x = (torch.randn((1, H), generator=g, device=DEV) * 0.5).to(torch.bfloat16)
+        ids = torch.rand((1, E), generator=g, device=DEV).topk(TOPK).indices.to(torch.int32)
+        tw = torch.softmax(torch.randn((1, TOPK), generator=g, device=DEV), -1)
+        return x, ids, tw
+
+    x, ids, tw = (t.clone() for t in draw())
+    for _ in range(2):  # eager warm-up: Triton compilation, tables
+        for m in layers:
+            m.forward_modular(x, tw, ids)
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s), torch.cuda.graph(graph, stream=s):
+        # Any torch operation that would synchronise with the host raises here.
+        torch.cuda.set_sync_debug_mode("error")
+        try:
+            outs = [m.forward_modular(x, tw, ids) for m in layers]
+        finally:
+            torch.cuda.set_sync_debug_mode("default")
+    torch.cuda.synchronize()
+    for step in range(10):
+        nx, nids, ntw = draw()
+        x.copy_(nx)
+        ids.copy_(nids)
+        tw.copy_(ntw)
+        graph.replay()
+        torch.cuda.synchronize()
+        for layer, out in enumerate(outs):
+            (w13, s13), (w2, s2) = weights[layer]["w13_weight"], weights[layer]["w2_weight"]
+            ref = torch.empty_like(x)
+            moe.moe_sum(moe.contributions(x, w13, w2, s13, s2, tw, ids, None, E, config), ref)
+            assert torch.equal(out, ref), f"replay {step} layer {layer}"
+    del graph
+    assert ex._store.failed is None and ex._store.reads > 0
+    assert all(m._expert_pager.step_errors() == 0 for m in layers)
 
 
 def test_hook_rejects_unsupported_setups(experts_mod, monkeypatch):

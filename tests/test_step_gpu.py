@@ -148,3 +148,51 @@ def test_host_ids_and_host_map_match_device_ids(tmp_path, compress, R):
     finally:
         sa.release()
         sb.release()
+
+
+def test_step_refuses_more_ctas_than_fit_at_once(tmp_path):
+    """The copy CTAs wait for the table and fetch CTAs, so a grid that cannot be
+    resident all at once is refused (XP_ERANGE) instead of timing out."""
+    from vllm_expert_pager import gather, synthetic
+
+    experts = synthetic.fp8_experts_device(E, DEV, seed=6)
+    store, pager = build(tmp_path, "c", False, 16, experts)
+    ids = torch.arange(S, dtype=torch.int32, device=DEV).view(1, -1)
+    saved = gather.GATHER_CTAS
+    try:
+        gather.GATHER_CTAS = 1024  # 1027 CTAs of 256 threads with the tables' shared memory
+        with pytest.raises(ValueError, match="-34"):
+            pager.decode(ids)
+        gather.GATHER_CTAS = 32
+        pager.decode(ids)
+        torch.cuda.synchronize()
+        assert pager.step_errors() == 0
+    finally:
+        gather.GATHER_CTAS = saved
+        store.release()
+
+
+def test_step_give_ups_reach_the_host_copy_and_the_hook_check(tmp_path):
+    """A step whose SSD-flag wait runs out (1 ms limit, host server delayed) counts
+    the give-ups in the pinned host copy that step_errors() reads without a sync."""
+    from vllm_expert_pager import native, synthetic
+
+    experts = synthetic.fp8_experts_device(E, DEV, seed=7)
+    store, pager = build(tmp_path, "e", True, 16, experts)
+    lib = native.lib()
+    try:
+        store.retry_ns = 2_000_000_000  # the fetch CTA itself neither re-publishes nor gives up
+        store.test_delay(0.3)
+        assert lib.xp_set_step_wait_ns(-1, 1_000_000) == native.XP_OK
+        ids = torch.arange(16, 16 + S, dtype=torch.int32, device=DEV).view(1, -1)  # RAM misses
+        pager.decode(ids)
+        torch.cuda.synchronize()
+        n = pager.step_errors()
+        # Concurrent give-ups may store their counts out of order: the host copy
+        # can lag the device counter, but it moved.
+        assert 0 < n <= int(pager.step_scratch[3])
+        assert store.failed is None
+    finally:
+        lib.xp_set_step_wait_ns(-1, -1)
+        store.test_delay(0.0)
+        store.release()

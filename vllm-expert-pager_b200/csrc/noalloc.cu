@@ -19,14 +19,23 @@
 // with XP_ERANGE before anything is launched.
 //
 // Host code cannot use the array's name as an address: the first call on each
-// device looks the address up with cudaGetSymbolAddress (with that device
-// current) and clears the flag block with cudaMemset, both synchronous, so
-// that first call should come before any stream capture.  Later calls reuse
-// the address.  Every call on a device shares the one array and finds the
-// previous call's contents in it: the step kernel leaves the flags at zero
-// (except its give-up counter, word 3), and the staging rows are fully
+// device looks the address up with cudaGetSymbolAddress, with that device
+// current (this may load the library's device code, so that first call should
+// come before any stream capture), and queues a clear of the flag block on the
+// call's stream, ahead of the kernels the call launches there.  Later calls
+// reuse the address, which stays valid for the life of the device's primary
+// context: do not call this entry point again after cudaDeviceReset.  Every
+// call on a device shares the one array and finds the previous call's contents
+// in it: the step kernel leaves the flags at zero (except its give-up counter,
+// word 3, which keeps counting across calls), and the staging rows are fully
 // rewritten by each call.  Two calls whose work overlaps on the GPU (different
 // streams, no ordering between them) race on the array.
+//
+// A wait of the step that gives up leaves stale staging rows, which the decode
+// then expands into slots the tables mark as filled.  The caller learns of it
+// through errors_out: when a wait gives up, the kernel stores the running
+// give-up count there (device memory, or mapped pinned host memory that the
+// host can poll without synchronising).
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -37,14 +46,19 @@ namespace {
 
 constexpr size_t kFlagsBytes = 256;
 constexpr int kMaxDevices = 128;
+// Staging words that fit after the flag block.
+constexpr int64_t kRoomWords = (static_cast<int64_t>(XP_NOALLOC_SCRATCH_BYTES) - 256) / 4;
+constexpr int64_t kMaxRows = 2048;  // the step kernel's list limit
 
 static __device__ __align__(256) unsigned char g_scratch[XP_NOALLOC_SCRATCH_BYTES];
 
 std::mutex g_mu;
 unsigned char *g_addr[kMaxDevices];
 
-// The device address of g_scratch on the current device (set up on first use).
-int scratch_address(unsigned char **out) {
+// The device address of g_scratch on the current device.  On the first use on
+// a device the address is looked up and a clear of the flag block is queued on
+// `stream`.
+int scratch_address(unsigned char **out, cudaStream_t stream) {
   int dev = -1;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return static_cast<int>(err);
@@ -54,7 +68,7 @@ int scratch_address(unsigned char **out) {
     void *p = nullptr;
     err = cudaGetSymbolAddress(&p, g_scratch);
     if (err != cudaSuccess) return static_cast<int>(err);
-    err = cudaMemset(p, 0, kFlagsBytes);
+    err = cudaMemsetAsync(p, 0, kFlagsBytes, stream);
     if (err != cudaSuccess) return static_cast<int>(err);
     g_addr[dev] = static_cast<unsigned char *>(p);
   }
@@ -76,16 +90,18 @@ extern "C" int xp_decode_step_noalloc(
     const void *scale0, void *sdst0, int64_t SW0, const void *scale1, void *sdst1, int64_t SW1,
     int compress, const uint8_t *lut, int64_t chunk, int ctas, int64_t layer, int64_t *seq,
     int64_t *req, const int64_t *done, int64_t block, int64_t ring, int64_t retry_ns,
-    int64_t giveup, void *stream) {
+    int64_t giveup, uint32_t *errors_out, void *stream) {
   if (K < 0 || P0 < 0 || P1 < 0 || W0 < 0 || W1 < 0) return XP_EINVAL;
   // Staging rows are P words each; keep every row 16-byte aligned.
   if (compress && ((P0 * 4) % 16 || (P1 * 4) % 16)) return XP_EINVAL;
+  // Bound each factor before multiplying, so K x (P0 + P1) x 4 cannot wrap.
+  if (K > kMaxRows || (compress && (P0 > kRoomWords || P1 > kRoomWords))) return XP_ERANGE;
   const int64_t stage0 = compress ? K * P0 * 4 : 0, stage1 = compress ? K * P1 * 4 : 0;
-  if (static_cast<uint64_t>(stage0) + static_cast<uint64_t>(stage1) + kFlagsBytes >
-      static_cast<uint64_t>(XP_NOALLOC_SCRATCH_BYTES))
+  if (stage0 + stage1 + static_cast<int64_t>(kFlagsBytes) >
+      static_cast<int64_t>(XP_NOALLOC_SCRATCH_BYTES))
     return XP_ERANGE;
   unsigned char *scratch = nullptr;
-  int rc = scratch_address(&scratch);
+  int rc = scratch_address(&scratch, static_cast<cudaStream_t>(stream));
   if (rc != XP_OK) return rc;
   unsigned char *stg0 = compress ? scratch + kFlagsBytes : nullptr;
   unsigned char *stg1 = compress ? scratch + kFlagsBytes + stage0 : nullptr;
@@ -95,7 +111,7 @@ extern "C" int xp_decode_step_noalloc(
                       b_counters, b_slots, b_slot, b_todo, no_cache, base, src0, dst0, stg0, W0,
                       P0, src1, dst1, stg1, W1, P1, scale0, sdst0, SW0, scale1, sdst1, SW1,
                       compress, ctas, layer, seq, req, done, block, ring, retry_ns, giveup,
-                      reinterpret_cast<uint32_t *>(scratch), stream);
+                      reinterpret_cast<uint32_t *>(scratch), errors_out, stream);
   if (rc != XP_OK || !compress || K == 0) return rc;
   return xp_decode_rows(a_todo, K, a_slot, no_cache, lut, stg0, P0 * 4, dst0, W0 * 4, stg1,
                         P1 * 4, dst1, W1 * 4, nullptr, chunk, stream);

@@ -14,12 +14,17 @@
 //                   this one expands every miss);
 //   last CTA        (when there is an SSD tier) waits for the tables, publishes
 //                   the request, waits for the host, raises the "ssd" flag.
-// The grid is a few dozen CTAs, all resident at once, so the waiting CTAs
-// never block the ones they wait for.  Every wait is bounded: after
-// `wait_ns` a CTA gives up, counts an error in scratch[3] and skips its work.
+// The grid is a few dozen CTAs; the launch is refused (XP_ERANGE) unless all of
+// them fit on the GPU at once (occupancy x SM count), so the waiting CTAs never
+// hold the SMs that the CTAs they wait for need.  Every wait is bounded: after
+// its limit a CTA gives up, counts an error in scratch[3] (and, if the caller
+// gave one, writes the new count to errors_out) and skips its work.
 // The scratch block (XP_STEP_SCRATCH_BYTES) holds the flags and a finished
 // counter; the last CTA to finish clears them, so every launch starts from
 // zero and the launch replays from a CUDA graph.
+#include <atomic>
+#include <mutex>
+
 #include "gather_dev.cuh"
 #include "table_dev.cuh"
 
@@ -48,6 +53,7 @@ struct StepArgs {
   int fetch;
   gdev::Fetch f;
   uint32_t *scratch;  // [0] tables done, [1] ssd done, [2] CTAs finished, [3] errors
+  uint32_t *errors_out;  // optional: receives the error count when a wait gives up
   int64_t table_wait_ns, ssd_wait_ns;
 };
 
@@ -57,9 +63,13 @@ __device__ __forceinline__ uint32_t load_acquire_gpu(const uint32_t *p) {
   return v;
 }
 
-// Thread 0 waits (bounded) until *flag >= target; true on every thread if it did.
+// Thread 0 waits (bounded) until *flag >= target; true on every thread if it
+// did.  A wait that gives up adds one to *errors and, if errors_out is set,
+// stores the new count there at system scope (it may be mapped host memory
+// that the host polls); concurrent give-ups may store their counts out of
+// order, so errors_out can lag *errors but moves whenever a wait gives up.
 __device__ bool wait_flag(const uint32_t *flag, uint32_t target, int64_t limit_ns,
-                          uint32_t *errors) {
+                          uint32_t *errors, uint32_t *errors_out) {
   __shared__ int s_ok;
   if (threadIdx.x == 0) {
     const uint64_t t0 = global_ns();
@@ -69,7 +79,11 @@ __device__ bool wait_flag(const uint32_t *flag, uint32_t target, int64_t limit_n
       __nanosleep(128);
     }
     s_ok = v >= target;
-    if (!s_ok) atomicAdd(errors, 1u);
+    if (!s_ok) {
+      const uint32_t n = atomicAdd(errors, 1u) + 1u;
+      if (errors_out)
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(errors_out), "r"(n) : "memory");
+    }
     __threadfence();
   }
   __syncthreads();
@@ -106,7 +120,7 @@ __global__ void __launch_bounds__(gdev::kThreads) step_kernel(const __grid_const
     if (vram && p.map_host)
       for (int64_t e = threadIdx.x; e < p.E; e += blockDim.x) p.map_host[e] = p.map32[e];
   } else if (p.fetch && role == static_cast<int>(gridDim.x) - 1) {
-    if (wait_flag(&flags[0], 2, p.table_wait_ns, &flags[3])) {
+    if (wait_flag(&flags[0], 2, p.table_wait_ns, &flags[3], p.errors_out)) {
       gdev::fetch_publish(p.f);
       __syncthreads();
       gdev::fetch_wait(p.f);
@@ -114,9 +128,9 @@ __global__ void __launch_bounds__(gdev::kThreads) step_kernel(const __grid_const
     raise_flag(&flags[1]);
   } else {
     const int cta = role - 2;
-    if (wait_flag(&flags[0], 2, p.table_wait_ns, &flags[3])) {
+    if (wait_flag(&flags[0], 2, p.table_wait_ns, &flags[3], p.errors_out)) {
       gdev::copy_rows<VEC>(p.ram, cta, p.copy_ctas, csm);
-      if (p.fetch && wait_flag(&flags[1], 1, p.ssd_wait_ns, &flags[3])) {
+      if (p.fetch && wait_flag(&flags[1], 1, p.ssd_wait_ns, &flags[3], p.errors_out)) {
         __syncthreads();
         gdev::copy_rows<VEC>(p.ssd, cta, p.copy_ctas, csm);
       }
@@ -135,10 +149,53 @@ __global__ void __launch_bounds__(gdev::kThreads) step_kernel(const __grid_const
   }
 }
 
+// Limits of the flag waits (xp_set_step_wait_ns); negative = the defaults.
+std::atomic<int64_t> g_table_wait_ns{-1}, g_ssd_wait_ns{-1};
+constexpr int64_t kDefaultTableWaitNs = 2'000'000'000;
+
+// Most step CTAs that fit on the current device at once, for one kernel and
+// dynamic shared memory size (cached: the occupancy query costs microseconds).
+int resident_ctas(const void *fn, size_t smem, int *out) {
+  struct Entry {
+    int dev;
+    const void *fn;
+    size_t smem;
+    int ctas;
+  };
+  static std::mutex mu;
+  static Entry cache[32];
+  static int used = 0;
+  int dev = -1;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return static_cast<int>(err);
+  std::lock_guard<std::mutex> lk(mu);
+  for (int i = 0; i < used; ++i)
+    if (cache[i].dev == dev && cache[i].fn == fn && cache[i].smem == smem) {
+      *out = cache[i].ctas;
+      return XP_OK;
+    }
+  int per_sm = 0, sms = 0;
+  err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, gdev::kThreads, smem);
+  if (err != cudaSuccess) return static_cast<int>(err);
+  err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (err != cudaSuccess) return static_cast<int>(err);
+  *out = per_sm * sms;
+  cache[used % 32] = Entry{dev, fn, smem, *out};
+  used = used < 32 ? used + 1 : 32;
+  return XP_OK;
+}
+
 }  // namespace
 }  // namespace xp
 
 using namespace xp;
+
+extern "C" int xp_set_step_wait_ns(int64_t table_ns, int64_t ssd_ns) {
+  if (table_ns > XP_MAX_RETRY_NS || ssd_ns > XP_MAX_RETRY_NS) return XP_EINVAL;
+  g_table_wait_ns.store(table_ns < 0 ? -1 : table_ns);
+  g_ssd_wait_ns.store(ssd_ns < 0 ? -1 : ssd_ns);
+  return XP_OK;
+}
 
 extern "C" int xp_decode_step(
     const void *topk_ids, int ids_bytes, int64_t K, int64_t E,
@@ -153,7 +210,7 @@ extern "C" int xp_decode_step(
     const void *scale0, void *sdst0, int64_t SW0, const void *scale1, void *sdst1, int64_t SW1,
     int compress, int ctas, int64_t layer, int64_t *seq, int64_t *req, const int64_t *done,
     int64_t block, int64_t ring, int64_t retry_ns, int64_t giveup, uint32_t *scratch,
-    void *stream) {
+    uint32_t *errors_out, void *stream) {
   StepArgs p{};
   p.ids = topk_ids;
   p.ids_bytes = ids_bytes;
@@ -208,8 +265,11 @@ extern "C" int xp_decode_step(
     p.f = gdev::Fetch{b_todo, K, b_slot, base, layer, seq, seq, req, done, block, ring,
                       retry_ns, giveup};
   p.scratch = scratch;
-  p.table_wait_ns = 2'000'000'000;
-  p.ssd_wait_ns = (giveup + 2) * retry_ns + 2'000'000'000;
+  p.errors_out = errors_out;
+  const int64_t tw = g_table_wait_ns.load(), sw = g_ssd_wait_ns.load();
+  p.table_wait_ns = tw >= 0 ? tw : kDefaultTableWaitNs;
+  // By default the copy CTAs outwait the fetch CTA's own bound on its SSD wait.
+  p.ssd_wait_ns = sw >= 0 ? sw : (giveup + 2) * retry_ns + kDefaultTableWaitNs;
   const int64_t S = a_slots > b_slots ? a_slots : b_slots;
   const size_t smem = tdev::table_smem_bytes(E, S);
   const unsigned grid = static_cast<unsigned>(2 + p.copy_ctas + (p.fetch ? 1 : 0));
@@ -220,6 +280,11 @@ extern "C" int xp_decode_step(
                                            static_cast<int>(smem));
     if (err != cudaSuccess) return static_cast<int>(err);
   }
+  // The copy CTAs wait for CTAs 0/1 and the fetch CTA: all must fit at once.
+  int fit = 0;
+  const int orc = resident_ctas(fn, smem, &fit);
+  if (orc != XP_OK) return orc;
+  if (static_cast<int64_t>(grid) > fit) return XP_ERANGE;
   if (vec)
     step_kernel<true><<<grid, gdev::kThreads, smem, s>>>(p);
   else

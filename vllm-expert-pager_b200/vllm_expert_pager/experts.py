@@ -29,7 +29,8 @@ from vllm.model_executor.layers.fused_moe.routed_experts import RoutedExperts
 from vllm_expert_pager.pager import PARAMS, LayerPager, WorkingSlab
 from vllm_expert_pager.store import Store
 
-# vLLM configures handlers only under the "vllm" logger (experts.py:33-37).
+# A logger outside the "vllm." namespace inherits the root's WARNING level in
+# vLLM's logging setup and drops info lines (experts.py:33-37).
 logger = init_logger(f"vllm.{__name__}")
 
 CACHE_SLOTS = int(os.environ.get("VLLM_EXPERT_PAGER_CACHE_SLOTS", "32"))
@@ -42,8 +43,9 @@ LOG_INTERVAL = int(os.environ.get("VLLM_EXPERT_PAGER_LOG_INTERVAL", "1000"))
 OVERLAP = os.environ.get("VLLM_EXPERT_PAGER_OVERLAP", "1") not in ("0", "false", "off")
 
 _store: Store | None = None
-# The working slab is shared by all layers; layers run one after another on
-# one stream, so no two layers use it at once (experts.py:79-83).
+# One WorkingSlab serves every layer.  vLLM calls the MoE layers in order on a
+# single stream, so a layer's chunk loop never overlaps another layer's
+# (experts.py:79-83).
 _working: WorkingSlab | None = None
 
 
@@ -93,8 +95,9 @@ class ExpertPagerRoutedExperts(RoutedExperts):
                 num_layers=get_current_vllm_config().model_config.hf_text_config.num_hidden_layers,
                 num_experts=E,
                 ram_slots=R,
-                # Two faces of shared working rows: chunk k+1 reads into the
-                # face whose copies finished with chunk k-1.
+                # RAM-tier rows for the SSD reads of the working path: 2 x W, so
+                # that the reads of one chunk never land in rows whose previous
+                # contents an earlier chunk is still copying to the GPU.
                 working_rows=2 * WORKING_ROWS,
                 row_bytes={n: p[0].numel() * p.element_size() for n, p in params.items()},
                 compress=compress,
@@ -105,7 +108,8 @@ class ExpertPagerRoutedExperts(RoutedExperts):
         self._expert_pager_store = _store
         self._expert_pager_layer = _store.add_layer()
 
-        # Compression assumes raw fp8 rows; Marlin repacks the exponent bits.
+        # The codec splits each fp8 byte into its exponent and sign/mantissa
+        # bits; weights in Marlin's repacked layout break that assumption.
         if _store.compress and (
             getattr(self.quant_method, "fp8_backend", None) == Fp8MoeBackend.MARLIN
         ):
@@ -113,11 +117,13 @@ class ExpertPagerRoutedExperts(RoutedExperts):
                 f"{self.layer_name}: vllm-expert-pager compresses raw fp8 rows and "
                 "does not support the MARLIN backend; set VLLM_EXPERT_PAGER_COMPRESS=off"
             )
-        # Keep only the shape of the (E, ...) weights; process_weights_after_loading
-        # sees E rows through a stride-0 expand (experts.py:160-167).
+        # The weights are paged, so the layer keeps a single real row per param;
+        # a stride-0 view makes it look [E, ...] to process_weights_after_loading
+        # (experts.py:160-167), and _expert_pager_setup trims it back.
         for p in params.values():
             p.data = torch.empty((1, *p.shape[1:]), dtype=p.dtype, device=p.device).expand(p.shape)
-        # w13 arrives as separate gate and up shards; stage per expert.
+        # The loader delivers w1 (gate) and w3 (up) separately; their halves of
+        # an expert's w13 row are collected here until the row is complete.
         self._expert_pager_stage: dict[int, tuple[torch.Tensor, set[str]]] = {}
 
         original = self.quant_method.process_weights_after_loading
@@ -147,7 +153,7 @@ class ExpertPagerRoutedExperts(RoutedExperts):
                 expert_id,
                 (torch.empty((2 * N, H), dtype=loaded_weight.dtype, device="cpu"), set()),
             )
-            half = 0 if shard_id == "w1" else N  # gate first, up second
+            half = 0 if shard_id == "w1" else N  # w13 row = [w1; w3]
             buf[half : half + N].copy_(loaded_weight)
             seen.add(shard_id)
             if seen != {"w1", "w3"}:
@@ -221,6 +227,12 @@ class ExpertPagerRoutedExperts(RoutedExperts):
         store = self._expert_pager_store
         if store.failed is not None:
             raise RuntimeError(f"vllm-expert-pager: SSD read failed\n{store.failed}")
+        gave_up = self._expert_pager.step_errors()
+        if gave_up:
+            raise RuntimeError(
+                f"vllm-expert-pager: {self.layer_name}: {gave_up} wait(s) of the decode step "
+                "gave up, so its slab holds stale rows"
+            )
         if topk_ids.numel() > self._expert_pager.cache_slots:
             return self._expert_pager_forward_working(x, topk_weights, topk_ids, shared_experts,
                                                       shared_experts_input)
@@ -309,6 +321,10 @@ class ExpertPagerRoutedExperts(RoutedExperts):
                 1e3 * store.io_seconds / store.fetches, int(store.req[store.retry_at]),
                 int(store.req[store.giveup_at]), store.missed,
             )  # fmt: skip
+        gave_up = self._expert_pager.step_errors()
+        if gave_up:
+            logger.warning("vllm-expert-pager %s: %d decode-step wait(s) gave up",
+                           self.layer_name, gave_up)
 
 
 def register() -> None:

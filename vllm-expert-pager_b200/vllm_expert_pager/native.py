@@ -51,7 +51,9 @@ _SIGNATURES = {
                               _p, _p, _p, _i64, _i64,
                               _p, _p, _p, _i64, _i64,
                               _p, _p, _i64, _p, _p, _i64,
-                              _i32, _i32, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _p]),
+                              _i32, _i32, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _p,
+                              _p]),
+    "xp_set_step_wait_ns": (_i32, [_i64, _i64]),
     "xp_decode_step_noalloc": (_i32, [_p, _i32, _i64, _i64,
                                       _p, _p, _p, _p, _i64, _p, _p, _p,
                                       _p, _p, _p, _p, _i64, _p, _p,
@@ -60,7 +62,7 @@ _SIGNATURES = {
                                       _p, _p, _i64, _i64,
                                       _p, _p, _i64, _p, _p, _i64,
                                       _i32, _p, _i64, _i32, _i64, _p, _p, _p, _i64, _i64, _i64,
-                                      _i64, _p]),
+                                      _i64, _p, _p]),
     "xp_decode_rows": (_i32, [_p, _i64, _p, _p, _p, _p, _i64, _p, _i64, _p, _i64, _p, _i64, _p,
                               _i64, _p]),
     "xp_encode_row": (_i32, [_p, _i64, _i64, _i64, _p, _p, ctypes.POINTER(_i64)]),

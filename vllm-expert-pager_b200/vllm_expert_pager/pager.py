@@ -128,6 +128,10 @@ class LayerPager:
         # Flags of the fused decode step (zero between launches; word 3 counts
         # waits that gave up).
         self.step_scratch = torch.zeros((4,), dtype=torch.int32, device=device)
+        # Pinned host copy of that count, stored by the kernel when a wait gives
+        # up; the host reads it without synchronising (graph replays included).
+        self.step_errors_host = torch.zeros((1,), dtype=torch.int32, pin_memory=True)
+        self._step_errors_np = self.step_errors_host.numpy()
 
     # ---- decode (experts.py:380-453) ----
 
@@ -227,7 +231,8 @@ class LayerPager:
                 int(store.compress), gather_mod.GATHER_CTAS, layer,
                 store.seq.data_ptr() if fetch else None, store.req_dev if fetch else None,
                 store.done_dev if fetch else None, store.block, store.ring, store.retry_ns,
-                store.giveup, self.step_scratch.data_ptr(), native.stream_of(store.device),
+                store.giveup, self.step_scratch.data_ptr(), self.step_errors_host.data_ptr(),
+                native.stream_of(store.device),
             ),
             "decode_step",
         )  # fmt: skip
@@ -240,8 +245,11 @@ class LayerPager:
         return DecodeResult(self.cache_slab, self.expert_map)
 
     def step_errors(self) -> int:
-        """Waits of the fused decode step that gave up (host read; not during capture)."""
-        return int(self.step_scratch[3])
+        """Waits of the fused decode step that gave up so far (a step with one holds
+        stale rows).  Reads the pinned host copy the kernel keeps: no device
+        synchronisation, so it is safe between graph replays and during capture,
+        and it may miss a give-up of a step still running on the GPU."""
+        return int(self._step_errors_np[0])
 
     # ---- working path (experts.py:455-577) ----
 

@@ -39,8 +39,8 @@ from vllm_expert_pager import codec, native
 
 logger = logging.getLogger(f"vllm.{__name__}")
 
-# Alignment required by O_DIRECT.  Rows, records and the pinned base address
-# are multiples of this.
+# Page size.  O_DIRECT reads need page-aligned offsets, lengths and buffers, so
+# the pinned tier's base, every row pitch and every record are whole pages.
 _ALIGN = 4096
 # Threads that read the experts of one layer concurrently (the server itself
 # and the workers): 8 as in the reference (store.py:59-64), which measured an
@@ -172,14 +172,17 @@ class Store:
             b = self._alloc(self.rows * nbytes)
             self.pinned[name] = b.cpu[: self.rows * nbytes].view(torch.int32).view(self.rows, -1)
             self.view[name] = b.cuda[: self.rows * nbytes].view(torch.int32).view(self.rows, -1)
-        # Per-row Huffman LUTs lut[l, e, i] (unused without compression).
+        # Decode tables, 512 bytes per (layer, expert, name); with raw rows
+        # only a single layer's worth exists, so the kernels still get a pointer.
         self.lut = torch.zeros(
             (L if compress else 1, E, len(self.names), codec.LUT_BYTES),
             dtype=torch.uint8, device=self.device,
         )  # fmt: skip
 
-        # req = [re-publishes, give-ups] + RING slots of [seq, layer, expert[B],
-        # row[B]] with B the power of two >= E (store.py:434-451).
+        # The request ring, in pinned host memory (store.py:434-451): two
+        # counters (re-publishes, give-ups), then RING request slots, each
+        # holding seq and layer followed by B expert ids and B RAM rows, where B
+        # is E rounded up to a power of two; done[0] follows the ring.
         self.block = 1 << (E - 1).bit_length()
         self.ring = RING
         self.retry_at, self.giveup_at = 0, 1
