@@ -1,26 +1,36 @@
 """Benchmark of the expert-paging hot path on B200 (one JSON line on rank 0).
 
-Workload ("single MoE layer decode paging"): 256 FP8
-experts of 3 MiB (w13 [1024, 2048] + w2 [2048, 512], N(0, 0.02) quantised with
-128x128 block scales), CACHE_SLOTS=32, RAM_SLOTS=256 uncompressed in pinned
-host memory, batch-1 top-8 routing drawn Zipf(1.1) over a seeded permutation
-(4096-step trace).  One bench step = one window of ``--window`` consecutive
-decode steps of the trace (512 by default, the 512 decode tokens of config 3),
-each running the decode paging path: acquire (VRAM + RAM tables), gather of the
-missed rows from pinned RAM over the host link (+ the fused SSD-fetch CTA,
-idle here since every expert is in RAM), gather of the SSD misses.
+Headline (``value``, BASELINE.json config 2, "single MoE layer decode paging"):
+256 FP8 experts of 3 MiB (w13 [1024, 2048] + w2 [2048, 512], N(0, 0.02)
+quantised with 128x128 block scales), CACHE_SLOTS=32, RAM_SLOTS=256
+uncompressed in pinned host memory, batch-1 top-8 routing drawn Zipf(1.1) over
+a seeded permutation (4096-step trace).  One bench step = one window of
+``--window`` consecutive decode steps of the trace (512 by default), each one
+fused launch: both LRU table updates, the gather of the missed rows from pinned
+RAM over the host link (+ the SSD-fetch CTA, idle here).
 
-  value   = bytes paged in (misses x 3 MiB) / device time of the timed steps,
-            summed over ranks (independent replicas, weak scaling)
-  e2e     = the same through the public API, host-driven: every decode step
-            reads its routing ids from pinned host memory and writes its
-            expert_map back to pinned host memory (by the step kernel itself)
-  roofline: the gather kernel's achieved host-link GB/s (algorithmic bytes /
-            CUDA-event duration of its launches) against the pinned-H2D copy
-            bandwidth measured here with the copy engine
+  value    = bytes paged in (misses x 3 MiB) / device time of the timed steps,
+             summed over ranks (independent replicas, weak scaling)
+  e2e      = the same through the public API, host-driven: every decode step
+             reads its routing ids from pinned host memory and writes its
+             expert_map back to pinned host memory (by the step kernel itself)
+  roofline = the step kernel's achieved host-link GB/s (algorithmic bytes /
+             CUDA-event duration of its launches) against the pinned-H2D copy
+             bandwidth measured here with the copy engine
+  links    = per rank: that copy bandwidth with the link idle and with every
+             rank copying, the RAM tier's NUMA node, the GPU's PCI address
+  configs  = (one GPU) config 4, where gather and decode run together: the
+             40-layer paged MoE with the compressed RAM tier (R=128) and the
+             O_DIRECT paging file at batch 1 and 8 under CUDA graphs, each with
+             the in-run host-link roofline of its copy kernel, the in-run HBM
+             roofline of the decode kernel and the SSD rate vs the disk's peak
+  kernels  = decode / acquire / encode kernels alone, and the reference's own
+             Triton kernels on the same inputs (a subprocess)
+  cpu_baseline = the reference's own CPU code (its ExpertTable on CPU tensors +
+             a threaded memcpy; a subprocess), the numpy port beside it, and
+             config 1's codec on the host cores
 
-``--impl reference`` times the reference algorithm's CPU restatement (oracle/):
-the LRU tables and a threaded memcpy of the same rows, on the host cores.
+``--impl reference`` times the reference's own CPU code (see run_reference).
 """
 
 from __future__ import annotations
@@ -64,6 +74,12 @@ def parse():
                         "on the inputs of paging/decode (one GPU)")
     p.add_argument("--layers", type=int, default=40, help="MoE layers of configs 3-5")
     p.add_argument("--tokens", type=int, default=512, help="decode tokens of configs 3-4")
+    p.add_argument("--c4-tokens", type=int, default=256,
+                   help="batch-1 decode tokens of the default line's config-4 entries "
+                        "(batch 8 runs a quarter as many steps)")
+    p.add_argument("--skip", default="",
+                   help="comma-separated parts of the default line to leave out: "
+                        "compressed, reference_triton, cpu, kernels")
     return p.parse_args()
 
 
@@ -200,8 +216,8 @@ def build_workload(device: torch.device):
     return store, pager, trace
 
 
-def measure_h2d_peak(device, world: int = 1) -> float:
-    """Copy-engine pinned->device bandwidth (GB/s), 1 GiB, best of 6.
+def measure_h2d_peak(device, world: int = 1, reps: int = 6) -> float:
+    """Copy-engine pinned->device bandwidth (GB/s), 1 GiB, best of ``reps``.
 
     With several ranks every rank copies at the same time (a barrier before each
     copy), so the figure is one replica's share of the host links and host memory
@@ -211,7 +227,7 @@ def measure_h2d_peak(device, world: int = 1) -> float:
     src = torch.empty(n, dtype=torch.uint8, pin_memory=True)
     dst = torch.empty(n, dtype=torch.uint8, device=device)
     best = 0.0
-    for _ in range(6):
+    for _ in range(reps):
         barrier(world)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
@@ -397,6 +413,15 @@ class PagedMoE:
         if store.fd_w is not None:
             os.fsync(store.fd_w)
         self.pool_weights = pw
+        # Mean used bytes of an expert's records (header + nibbles + Huffman words).
+        self.used_mean = float(sum(store.row_bytes.values()))
+        if compress:
+            used = 0
+            for (p, n), rec in recs.items():
+                N = store.row_bytes[n]
+                G = N // codec.GROUP
+                used += 4 * (G + 1) + N // 2 + 4 * int(rec[G])
+            self.used_mean = used / pool
         shapes = {n: (synthetic.SHAPES[n], torch.float8_e4m3fn) for n in PARAMS}
         all_shapes = dict(shapes)
         all_shapes.update({f"{n[:-7]}_weight_scale": (tuple(pw[n][1].shape[1:]), torch.float32)
@@ -419,7 +444,11 @@ class PagedMoE:
         return self.configs[T]
 
     def layer(self, l, h, events=None):
-        """One MoE layer with paged experts: route, page, run vLLM's fused MoE, add residual."""
+        """One MoE layer with paged experts: route, page, run vLLM's fused MoE, add residual.
+
+        ``events``: None, or a dict of lists that receive timing events of the
+        paging launches (``step``: the fused decode step; ``decode``: decode
+        launches; ``copy``: working-path gathers), as LayerPager records them."""
         moe, pager = self.moe, self.pagers[l]
         T = h.shape[0]
         logits = (h @ self.router[l]).float()
@@ -428,8 +457,9 @@ class PagedMoE:
         ids = ids.to(torch.int32)
         cfg = self.config(T)
         out = torch.empty_like(h)
+        ev = events or {}
         if ids.numel() <= self.S:
-            res = pager.decode(ids)
+            res = pager.decode(ids, gather_events=ev.get("step"), decode_events=ev.get("decode"))
             s = res.slabs
             c3 = moe.contributions(h, s["w13_weight"], s["w2_weight"], s["w13_weight_scale"],
                                    s["w2_weight_scale"], w, ids, res.expert_map, E, cfg)
@@ -445,12 +475,13 @@ class PagedMoE:
                 if k == n - 1:
                     moe.moe_sum(acc["c"], out)
 
-            pager.working_chunks(ids, run_chunk, overlap=self.overlap)
+            pager.working_chunks(ids, run_chunk, overlap=self.overlap,
+                                 decode_events=ev.get("decode"), copy_events=ev.get("copy"))
         return h + out
 
-    def forward(self, h):
+    def forward(self, h, events=None):
         for l in range(self.L):
-            h = self.layer(l, h)
+            h = self.layer(l, h, events)
         return h
 
     def misses(self) -> int:
@@ -486,13 +517,30 @@ def timed(fn, reps=1):
     return a.elapsed_time(b) / reps
 
 
-def run_model_decode(args, device, compress: bool, R: int, batch: int, tokens: int,
-                     path=None) -> dict:
-    """Configs 3 and 4: decode ``tokens`` tokens of a 40-layer paged MoE, graph-replayed."""
-    m = PagedMoE(device, layers=args.layers, S=S, R=R, compress=compress, path=path)
-    m.store.retry_ns = 500_000_000
-    gen = torch.Generator(device=device).manual_seed(11)
-    emb = (torch.randn((tokens + 16, batch, 2048), generator=gen, device=device) * 0.5).to(torch.bfloat16)
+def decode_row_bytes(m) -> float:
+    """Algorithmic bytes of expanding one expert of ``m``: the used record bytes read
+    (mean over the pool's records), the raw bytes written and the two 512-byte LUTs."""
+    raw = sum(m.store.row_bytes.values())
+    return m.used_mean + raw + 2 * 512
+
+
+def _sum_events(evs) -> tuple[float, int, int]:
+    """(total ms, rows, launches) of a list of (start, end, rows) timing triples."""
+    ms = sum(e[0].elapsed_time(e[1]) for e in evs)
+    rows = sum(int(e[2]) for e in evs)
+    return ms, rows, len(evs)
+
+
+def model_decode(m, device, batch: int, tokens: int, h2d_peak: float | None = None,
+                 probe: int = 8, seed: int = 11) -> dict:
+    """Configs 3 and 4: ``tokens`` decode steps of batch ``batch`` through the paged
+    MoE ``m``, replayed from one CUDA graph and timed with CUDA events; then ``probe``
+    more steps run eagerly with CUDA events around every paging launch, which give
+    the in-run rooflines of the copy and decode kernels (same model and tables, right
+    after the timed replays; the probe's layer steps are synchronised one by one so
+    that each fused step can be told apart by whether the host read the SSD for it)."""
+    gen = torch.Generator(device=device).manual_seed(seed)
+    emb = (torch.randn((16, batch, 2048), generator=gen, device=device) * 0.5).to(torch.bfloat16)
     x = torch.empty((batch, 2048), dtype=torch.bfloat16, device=device)
     x.copy_(emb[0])
     for t in range(3):  # eager warm-up (Triton JIT, tables)
@@ -511,8 +559,9 @@ def run_model_decode(args, device, compress: bool, R: int, batch: int, tokens: i
         x.copy_(emb[t])
         graph.replay()
     torch.cuda.synchronize()
-    miss0 = m.misses()
-    reads0 = m.store.reads
+    store = m.store
+    miss0, reads0 = m.misses(), store.reads
+    gu0 = int(store.req[store.giveup_at])
 
     def run():
         for t in range(tokens):
@@ -522,22 +571,95 @@ def run_model_decode(args, device, compress: bool, R: int, batch: int, tokens: i
     with Clocks(torch.cuda.current_device()) as clocks:
         ms = timed(run)
     misses = m.misses() - miss0
+    reads = store.reads - reads0
+    finite = bool(torch.isfinite(y).all())
+    del graph
     m.check()
-    res = {"layers": args.layers, "batch": batch, "tokens": tokens, "ms": round(ms, 2),
+    record = store.record_bytes if store.compress else EXPERT_BYTES
+    res = {"layers": m.L, "batch": batch, "tokens": tokens, "ms": round(ms, 2),
            "tok_per_s": round(tokens * batch / (ms * 1e-3), 2),
            "tpot_ms": round(ms / tokens, 3),
-           "paged_gb_per_s": round(misses * (m.store.record_bytes if compress else EXPERT_BYTES)
-                                   / (ms * 1e-3) / 1e9, 3),
-           "vram_misses_per_layer_step": round(misses / (tokens * args.layers), 3),
-           "ssd_reads": m.store.reads - reads0,
-           "ssd_gb_per_s": round((m.store.reads - reads0) * m.store.record_bytes
-                                 / (ms * 1e-3) / 1e9, 3),
-           "ssd_failed": m.store.failed,
-           "giveups": int(m.store.req[m.store.giveup_at]), "clocks": clocks.summary(),
-           "finite": bool(torch.isfinite(y).all())}
-    del graph
-    m.release()
+           "path": "decode (fused step)" if batch * TOPK <= m.S else "working slab (chunks)",
+           "ssd_reads": reads,
+           "ssd_gb_per_s": round(reads * record / (ms * 1e-3) / 1e9, 3),
+           "ssd_failed": store.failed,
+           "giveups": int(store.req[store.giveup_at]) - gu0,
+           "step_errors": sum(p.step_errors() for p in m.pagers),
+           "clocks": clocks.summary(), "finite": finite}
+    if batch * TOPK <= m.S:
+        res["paged_gb_per_s"] = round(misses * record / (ms * 1e-3) / 1e9, 3)
+        res["vram_misses_per_layer_step"] = round(misses / (tokens * m.L), 3)
+
+    # Probe: the same steps eagerly, with events around every paging launch.
+    ev = {"step": [], "decode": [], "copy": []}
+    steps = []  # per fused step: (misses, did the host read the SSD for it)
+    torch.cuda.synchronize()
+    for t in range(probe):
+        h = emb[t % 8].clone()
+        for layer in range(m.L):
+            pager = m.pagers[layer]
+            r0, n0 = store.reads, len(ev["step"])
+            c0 = int(pager.vram.counters[2])
+            h = m.layer(layer, h, ev)
+            torch.cuda.synchronize()
+            if len(ev["step"]) > n0:
+                steps.append((int(pager.vram.counters[2]) - c0, store.reads > r0))
+    hbm, hsrc = hbm_peak()
+    probe_res = {"tokens": probe * batch, "how": "eager steps after the timed replays; CUDA "
+                 "events around each paging launch on its stream; kernel times summed"}
+    if ev["decode"]:
+        d_ms, d_rows, d_n = _sum_events(ev["decode"])
+        per_row = decode_row_bytes(m)
+        ach = d_rows * per_row / (d_ms * 1e-3) / 1e9 if d_ms > 0 else 0.0
+        probe_res["decode"] = {
+            "kernel": "decode_ring_kernel", "bound": "hbm", "launches": d_n,
+            "rows_per_launch": round(d_rows / max(d_n, 1), 2),
+            "us_per_launch": round(1e3 * d_ms / max(d_n, 1), 2),
+            "algorithmic_bytes_per_row": int(per_row),
+            "bytes_how": "mean used record bytes of the pool's records + raw bytes + 2 LUTs",
+            "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
+            "frac": round(ach / hbm, 4), "peak_source": hsrc}
+    if ev["step"]:
+        t_all = [a.elapsed_time(b) for a, b in ev["step"]]
+        ram = [(ms_, n) for ms_, (n, ssd) in zip(t_all, steps) if not ssd and n > 0]
+        link = {"kernel": "step_kernel (both table updates + the copies of the misses; on "
+                          "steps that read the SSD it also waits for the host)",
+                "bound": "host_link", "launches": len(t_all),
+                "launches_with_ssd": sum(1 for _, ssd in steps if ssd), "unit": "GB/s"}
+        if ram:
+            b_ = sum(n for _, n in ram) * record
+            ach = b_ / (sum(ms_ for ms_, _ in ram) * 1e-3) / 1e9
+            link.update({"achieved": round(ach, 3),
+                         "how": "steps served from the RAM tier alone: record bytes of "
+                                "their misses / their step-kernel time"})
+            if h2d_peak:
+                link.update({"peak": round(h2d_peak, 3), "frac": round(ach / h2d_peak, 4)})
+        probe_res["host_link"] = link
+    if ev["copy"]:
+        c_ms, c_rows, c_n = _sum_events(ev["copy"])
+        ach = c_rows * record / (c_ms * 1e-3) / 1e9 if c_ms > 0 else 0.0
+        link = {"kernel": "gather_kernel (working path: RAM tier -> staging)",
+                "bound": "host_link", "launches": c_n, "rows": c_rows, "unit": "GB/s",
+                "achieved": round(ach, 3)}
+        if h2d_peak:
+            link.update({"peak": round(h2d_peak, 3), "frac": round(ach / h2d_peak, 4)})
+        probe_res["host_link"] = link
+        res["paged_gb_per_s"] = round(c_rows * record / (probe * batch) * res["tok_per_s"]
+                                      / 1e9, 3)
+        res["paged_gb_per_s_how"] = "record bytes per token of the probe steps x timed tok/s"
+    res["probe"] = probe_res
     return res
+
+
+def run_model_decode(args, device, compress: bool, R: int, batch: int, tokens: int,
+                     path=None) -> dict:
+    """Configs 3 and 4 as separate lines (``--workload model|compressed``)."""
+    m = PagedMoE(device, layers=args.layers, S=S, R=R, compress=compress, path=path)
+    m.store.retry_ns = 500_000_000
+    try:
+        return model_decode(m, device, batch, tokens)
+    finally:
+        m.release()
 
 
 def run_prefill(args, device, path) -> dict:
@@ -642,6 +764,80 @@ def disk_peak(path: str, record_bytes: int, seconds: float = 3.0) -> dict:
     best["how"] = ("random O_DIRECT preadv on the paging file, whole records or the server's "
                    "read-job size, 8 or 32 threads; the best")
     return best
+
+
+def compressed_configs(args, device, h2d_peak: float) -> dict:
+    """Config 4 in the default line: the 40-layer paged MoE with the compressed RAM tier
+    (R=128, pitch 0.89) and the O_DIRECT paging file, batch 1 (decode path: one fused
+    step + one decode launch per layer) and batch 8 (K=64 > S: every step on the
+    working slab), each replayed from a CUDA graph, with the in-run rooflines of the
+    copy and decode kernels and the SSD rate against the disk's own peak."""
+    base = os.environ.get("XP_BENCH_DIR", "/tmp")
+    path = os.path.join(base, f"xpager_bench_c4_{os.getpid()}.bin")
+    out = {}
+    m = None
+    try:
+        m = PagedMoE(device, layers=args.layers, S=S, R=128, compress=True, path=path)
+        m.store.retry_ns = 500_000_000
+        b1 = args.c4_tokens
+        out["compressed_b1"] = model_decode(m, device, 1, b1, h2d_peak)
+        out["compressed_b8"] = model_decode(m, device, 8, max(b1 // 4, 8), h2d_peak, probe=2)
+        peak = disk_peak(path, m.store.record_bytes)
+        for v in out.values():
+            if "gb_per_s" in peak:
+                v["ssd_frac_of_disk_peak"] = round(v["ssd_gb_per_s"] / peak["gb_per_s"], 3)
+        out["disk_peak"] = peak
+        out["model"] = (f"{args.layers} layers, hidden 2048, moe_inter 512, E=256, top-8, fp8 "
+                        "128x128 block scales, random-init routers; the 256 x layers experts are "
+                        "drawn from a pool of 64 seeded experts (every (layer, expert) is its own "
+                        "record in the RAM tier and the paging file); CACHE_SLOTS=32, "
+                        "RAM_SLOTS=128 compressed at pitch 0.89, O_DIRECT paging file")
+    finally:
+        if m is not None:
+            m.release()
+        if os.path.exists(path):
+            os.unlink(path)
+    return out
+
+
+def link_info(device, store, world: int, rank: int, concurrent: float) -> list[dict] | dict:
+    """This rank's host link: the pinned->device copy bandwidth with the link idle (the
+    ranks measure one after another), the figure with all ranks copying at once, the
+    NUMA node of its RAM tier and its GPU's PCI address.  Gathered to rank 0."""
+    idle = None
+    for r in range(world):
+        barrier(world)
+        if r == rank:
+            idle = measure_h2d_peak(device, 1, reps=3)
+    barrier(world)
+    p = torch.cuda.get_device_properties(device)
+    info = {"rank": rank, "pci_bus_id": f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:"
+                                       f"{p.pci_device_id:02x}.0",
+            "ram_tier_numa_node": store.numa_node, "h2d_idle_gb_s": round(idle, 3),
+            "h2d_concurrent_gb_s": round(concurrent, 3)}
+    if world == 1:
+        return [info]
+    import torch.distributed as dist
+
+    out = [None] * world
+    dist.all_gather_object(out, info)
+    return out
+
+
+def run_json_subprocess(argv: list[str], timeout: float) -> dict:
+    """Run ``bench.py`` with ``argv`` in a fresh process (no torchrun variables) and
+    return the last JSON line it printed, or {"unavailable": why}."""
+    env = {k: v for k, v in os.environ.items()
+           if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "MASTER_ADDR", "MASTER_PORT")}
+    try:
+        p = subprocess.run([sys.executable, os.path.abspath(__file__), *argv], env=env,
+                           capture_output=True, text=True, timeout=timeout)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": f"timed out after {timeout:.0f} s"}
+    for ln in reversed(p.stdout.strip().splitlines()):
+        if ln.startswith("{"):
+            return json.loads(ln)
+    return {"unavailable": f"rc {p.returncode}: {p.stderr.strip()[-300:]}"}
 
 
 def run_model_workload(args):
@@ -1118,44 +1314,145 @@ def run_reference_triton(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def config2(W: int, world: int) -> dict:
+    """The config of the headline line; both arms print this dict."""
+    return {"workload": "config2: single-layer decode paging, E=256 x 3 MiB, CACHE_SLOTS=32, "
+                        "RAM_SLOTS=256 raw, batch 1 top-8 Zipf(1.1), 4096-step trace",
+            "window": W, "parallelism": f"replicas x{world}",
+            "l2": "inputs larger than L2 (768 MiB pinned RAM tier read over the host link "
+                  "per replica)"}
+
+
+def reference_table_leg(trace: torch.Tensor, steps: int, ptrs, slab, threads: int,
+                        table_cls) -> tuple[float, float]:
+    """The reference's own decode-path tables on the host: its ``ExpertTable.acquire``
+    (table.py:75-128, torch ops on CPU tensors, as the reference's tests run it) on the
+    VRAM (S) and RAM (R) tables of every step, then a ``threads``-way memcpy of the
+    missed rows from the RAM tier into the slab (the reference's gather is a GPU kernel;
+    on the host the copy is a memcpy).  Returns (seconds, bytes copied)."""
+    from oracle import _lib as olib
+
+    cpu = torch.device("cpu")
+    vram, ram = table_cls(E, S, cpu), table_cls(E, R, cpu)
+    ram.slot_of[:R] = ram.experts[:R]
+    ram.expert_in[:R] = ram.experts[:R]
+    moved = 0
+    t0 = time.perf_counter()
+    for i in range(steps):
+        ids = trace[i % TRACE_STEPS]
+        _, slot, todo = vram.acquire(ids)
+        _, src, _ = ram.acquire(ids)
+        t = todo.numpy()
+        m = t[t >= 0]
+        if m.size:
+            dst_rows, src_rows = slot.numpy()[m], src.numpy()[m]
+            for k, (ptr, nbytes) in enumerate(ptrs):
+                olib.copy_rows(ptr, nbytes, src_rows, slab[k].ctypes.data, nbytes, dst_rows,
+                               nbytes, threads)
+            moved += m.size * EXPERT_BYTES
+    return time.perf_counter() - t0, moved
+
+
+def reference_codec_leg(syn, codec_mod, threads: int = 8) -> dict:
+    """The reference's ``codec.encode`` (codec.py:125-193, torch ops) of the 16 config-1
+    rows on CPU tensors with ``threads`` torch threads: raw MB/s."""
+    torch.set_num_threads(threads)
+    experts = syn.fp8_experts(8, seed=0)
+    raws = [syn.row_bytes(ex[n][0]) for ex in experts for n in syn.SHAPES]
+    codec_mod.encode(raws[0], codec_mod.pitch_of(raws[0].numel(), 0.89, 4096))  # warm-up
+    t0 = time.perf_counter()
+    for r in raws:
+        codec_mod.encode(r, codec_mod.pitch_of(r.numel(), 0.89, 4096))
+    dt = time.perf_counter() - t0
+    total = sum(r.numel() for r in raws)
+    return {"encode_mb_s": round(total / dt / 1e6, 1), "threads": threads, "kind": "reference",
+            "raw_mb": round(total / 1e6, 3),
+            "how": "the reference's codec.encode of the 16 config-1 rows (8 experts, pitch "
+                   "0.89) on CPU tensors"}
+
+
+def reference_install():
+    """The reference package installed under baseline/_ref, imported as
+    ``vllm_expert_pager`` (only in processes that never import this repository's
+    package), or None when it is not installed."""
+    if not os.path.isdir(os.path.join(REF_DIR, "vllm_expert_pager")):
+        return None
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    import vllm_expert_pager as refpkg
+
+    if not os.path.abspath(refpkg.__file__).startswith(REF_DIR):
+        raise SystemExit("vllm_expert_pager did not resolve to baseline/_ref")
+    return refpkg
+
+
 def run_reference(args, world, rank):
-    """--impl reference: the CPU restatement of the reference path on the host cores."""
+    """--impl reference: the reference's own CPU code for the path on the host cores.
+
+    Each step is one window of the config-2 trace through the reference's
+    ``ExpertTable.acquire`` on both tables (installed unmodified in baseline/_ref) and a
+    threaded memcpy of the missed rows (``reference_table_leg``).  Without the install,
+    the numpy restatement of the same algorithm under oracle/ stands in (kind "port").
+    The reference's ``codec.encode`` on config 1 is reported beside it."""
     if rank != 0:
         return
-    from vllm_expert_pager import synthetic
-
+    syn = _synthetic_by_path()
     threads = os.cpu_count() or 1
-    trace = synthetic.zipf_trace(TRACE_STEPS, E, TOPK, 1.1, layer=0).numpy()
-    row = {n: r * c for n, (r, c) in synthetic.SHAPES.items()}
+    trace = syn.zipf_trace(TRACE_STEPS, E, TOPK, 1.1, layer=0)
+    row = {n: r * c for n, (r, c) in syn.SHAPES.items()}
     src = {n: np.zeros((R, b), dtype=np.uint8) for n, b in row.items()}
     rng = np.random.default_rng(0)
     for n in src:
         src[n][:] = rng.integers(0, 256, src[n].shape, dtype=np.uint8)
     slab = [np.zeros((S, b), dtype=np.uint8) for b in row.values()]
     ptrs = [(src[n].ctypes.data, row[n]) for n in row]
+    ref = reference_install()
+    if ref is not None:
+        import vllm_expert_pager.codec as rcodec
+        from vllm_expert_pager.table import ExpertTable as RefTable
+
+        torch.set_num_threads(threads)
+
+        def leg(n):
+            return reference_table_leg(trace, n, ptrs, slab, threads, RefTable)
+        kind = "reference"
+        what = (f"the reference's ExpertTable.acquire (baseline/_ref, torch on CPU tensors) on "
+                f"both tables + {threads}-thread memcpy of the missed rows")
+    else:
+        tr = trace.numpy()
+
+        def leg(n):
+            return cpu_port(tr, n, ptrs, slab, threads)
+        kind = "port"
+        what = f"numpy restatement of the reference's tables + {threads}-thread memcpy"
     for _ in range(args.warmup):
-        cpu_port(trace, args.window, ptrs, slab, threads)
+        leg(args.window)
     secs, moved = 0.0, 0
     for _ in range(args.steps):
-        s, m = cpu_port(trace, args.window, ptrs, slab, threads)
-        secs += s
-        moved += m
+        sec, mv = leg(args.window)
+        secs += sec
+        moved += mv
     value = moved / secs / 1e9
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1e3 * secs / args.steps, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
-        "config": {"workload": "config2: single-layer decode paging, E=256 x 3 MiB, "
-                   "CACHE_SLOTS=32, RAM_SLOTS=256 raw, batch 1 top-8 Zipf(1.1)",
-                   "window": args.window},
+        "config": config2(args.window, world),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
-                         "kind": "port",
-                         "sample": f"{args.steps} windows of {args.window} trace steps"},
+                         "kind": kind,
+                         "sample": f"{args.steps} windows of {args.window} trace steps: {what}"},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
         "tok_per_s": round(args.window * args.steps / secs, 1),
     }
+    if ref is not None:
+        line["codec_config1"] = reference_codec_leg(syn, rcodec)
+        sample = min(args.window, 256)
+        ps, pm = cpu_port(trace.numpy(), sample, ptrs, slab, threads)
+        line["port"] = {"value": round(pm / ps / 1e9, 3), "unit": "GB/s", "cores": threads,
+                        "sample": f"first {sample} trace steps: numpy restatement of the "
+                                  "tables (oracle/) + the same memcpy"}
     print(json.dumps(line), flush=True)
 
 
@@ -1189,6 +1486,7 @@ def main():
         return
     if args.ctas:
         gather_mod.GATHER_CTAS = args.ctas
+    skip = set(filter(None, args.skip.split(",")))
     store, pager, trace_cpu = build_workload(device)
     trace = trace_cpu.to(device)
     W = args.window
@@ -1252,24 +1550,54 @@ def main():
     value, _, ms_max = aggregate(moved, ms, world)
     e2e, _, _ = aggregate(e_moved, e_ms, world)
     achieved = moved / (gather_ms * 1e-3) / 1e9 if gather_ms > 0 else None
+    links = link_info(device, store, world, rank, peak)
 
-    kernels = {"decode_k8": bench_decode(device, 8), "decode_k64": bench_decode(device, 64),
-               "acquire_pair": bench_acquire(device), "encode_gpu": bench_encode(device)}
+    kernels = {}
+    if "kernels" not in skip:
+        kernels = {"decode_k8": bench_decode(device, 8), "decode_k64": bench_decode(device, 64),
+                   "acquire_pair": bench_acquire(device), "encode_gpu": bench_encode(device)}
 
     cpu = None
-    if rank == 0 and world == 1:
+    if rank == 0 and world == 1 and "cpu" not in skip:
         threads = os.cpu_count() or 1
         names = list(store.pinned)
         ptrs = [(store.pinned[n].data_ptr(), store.pinned[n].shape[1] * 4) for n in names]
         slab = [np.zeros((S, store.pinned[n].shape[1] * 4), dtype=np.uint8) for n in names]
         tr = trace_cpu.numpy()
         sample = 256
-        secs, cm = cpu_port(tr, sample, ptrs, slab, threads)
-        cpu = {"value": round(cm / secs / 1e9, 3), "unit": "GB/s", "cores": threads,
-               "kind": "port",
-               "sample": f"first {sample} of {TRACE_STEPS} trace steps: numpy LRU tables + "
-                         f"{threads}-thread memcpy of the missed rows"}
+        psecs, pm = cpu_port(tr, sample, ptrs, slab, threads)
+        port = {"value": round(pm / psecs / 1e9, 3), "unit": "GB/s", "cores": threads,
+                "kind": "port",
+                "sample": f"first {sample} of {TRACE_STEPS} trace steps: numpy restatement of "
+                          f"the LRU tables + {threads}-thread memcpy of the missed rows"}
+        # The reference's own CPU code runs in a process of its own: both packages are
+        # named vllm_expert_pager.
+        ref = run_json_subprocess(["--impl", "reference", "--steps", "1", "--warmup", "1",
+                                   "--window", str(sample)], timeout=900)
+        if "value" in ref:
+            cb = ref["cpu_baseline"]
+            cpu = {"value": ref["value"], "unit": "GB/s", "cores": cb["cores"],
+                   "kind": cb["kind"], "sample": cb["sample"], "port": port}
+            if "codec_config1" in ref:
+                cpu["codec_config1_reference"] = ref["codec_config1"]
+        else:
+            cpu = dict(port)
+            cpu["reference_unavailable"] = ref.get("unavailable")
         cpu["codec_config1"] = codec_baselines(device)
+    if rank == 0 and world == 1 and "reference_triton" not in skip:
+        rt = run_json_subprocess(["--workload", "reference-triton", "--steps", "2", "--warmup",
+                                  "1", "--window", str(W)], timeout=900)
+        kernels["reference_triton"] = rt.get("kernels", rt)
+
+    # Config 4 (compressed tier, SSD, gather + GPU decode) on one GPU: its paging file
+    # takes ~29 GB of disk per rank, so the replica runs (N > 1) leave it out.
+    configs = None
+    if world == 1 and "compressed" not in skip:
+        del pager, trace, host_trace
+        store.release()
+        store = None
+        torch.cuda.empty_cache()
+        configs = compressed_configs(args, device, peak)
 
     if rank == 0:
         steps_total = args.steps * W
@@ -1278,11 +1606,7 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
             "data": "synthetic (seeded fp8 experts generated on the device; Zipf(1.1) trace)",
-            "config": {"workload": "config2: single-layer decode paging, E=256 x 3 MiB, "
-                       "CACHE_SLOTS=32, RAM_SLOTS=256 raw, batch 1 top-8 Zipf(1.1), 4096-step "
-                       "trace", "window": W, "parallelism": f"replicas x{world}",
-                       "l2": "inputs larger than L2 (768 MiB pinned RAM tier read over the host "
-                             "link per replica)"},
+            "config": config2(W, world),
             "tok_per_s": round(steps_total * world / (ms_max * 1e-3), 1),
             "miss_rate": round(misses / (steps_total * TOPK), 4),
             "e2e": {"value": round(e2e, 3), "unit": "GB/s", "h2d_bytes_per_step": W * TOPK * 4,
@@ -1290,14 +1614,17 @@ def main():
             "roofline": {"bound": "host_link", "achieved": round(achieved, 3) if achieved else None,
                          "peak": round(peak, 3), "unit": "GB/s",
                          "frac": round(achieved / peak, 4) if achieved else None,
-                         # Host-link bytes per average launch: an ncu capture of the step
-                         # kernel (--set full, three launches of this workload) read exactly
-                         # the algorithmic bytes over the link (sysmem sectors x 32 B), so
-                         # the measured ratio 1.0 applies; DRAM per launch from the same
-                         # capture.
-                         "traffic": int(moved / (args.steps * W)),
-                         "traffic_unit": "bytes per launch over the host link",
-                         "dram_bytes_per_launch": 87000,
+                         # From one ncu capture of three step-kernel launches of this
+                         # workload (profiles/step_kernel_config2.md): DRAM bytes per
+                         # launch, and the host-link bytes, which equalled the algorithmic
+                         # bytes exactly (sysmem sectors x 32 B = misses x 3 MiB).
+                         "traffic": 87000,
+                         "traffic_unit": "DRAM bytes per launch",
+                         "traffic_source": "ncu capture, profiles/step_kernel_config2.md "
+                                           "(--set full, 3 launches): dram read + write",
+                         "link_traffic_ratio": 1.0,
+                         "link_traffic_source": "same capture: host-link read sectors x 32 B "
+                                                "/ algorithmic bytes",
                          "kernel": "step_kernel (both table updates + the gather, one launch "
                                    "per decode step)",
                          "peak_source": "measured in bench.py: copy engine pinned->device, "
@@ -1305,11 +1632,14 @@ def main():
                                             f", all {world} ranks copying at once"
                                             if world > 1 else "") +
                                         " (MEASURED_PEAKS.json has no host-link figure)"},
+            "links": links,
             "kernels": kernels,
             "gpu_launches": args.steps * W,
             "cpu_baseline": cpu,
             "clocks": clocks.summary(),
         }
+        if configs is not None:
+            line["configs"] = configs
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist

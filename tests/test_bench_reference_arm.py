@@ -1,9 +1,12 @@
 """bench.py's reference arm on the CPU: one JSON line with the contract's keys.
 
-``bench.py --impl reference`` times the CPU restatement of the reference's paging
-path (numpy LRU tables + threaded memcpy) and needs no GPU, so its output line
-is checked here: the metric, unit and config of the GPU arm, a cpu_baseline
-block describing the sample, and an e2e block with no host<->device bytes.
+``bench.py --impl reference`` times the reference's own CPU code for the paging
+path -- its ``ExpertTable.acquire`` from the unmodified install under
+baseline/_ref on both tables, plus a threaded memcpy of the missed rows -- or,
+without the install, the numpy restatement under oracle/.  It needs no GPU, so
+its output line is checked here: the metric, unit and config of the GPU arm, a
+cpu_baseline block describing the sample, and an e2e block with no
+host<->device bytes.
 """
 
 import json
@@ -31,8 +34,13 @@ def test_reference_arm_prints_one_contract_line():
     assert d["ms_per_step"] > 0 and d["scaling"] == "weak" and d["vs_baseline"] is None
     assert d["config"]["workload"].startswith("config2")
     cb = d["cpu_baseline"]
-    assert cb["value"] == d["value"] and cb["kind"] == "port" and cb["cores"] >= 1
+    assert cb["value"] == d["value"] and cb["cores"] >= 1
     assert cb["unit"] == "GB/s" and cb["sample"]
+    ref_installed = os.path.isdir(os.path.join(ROOT, "baseline", "_ref", "vllm_expert_pager"))
+    assert cb["kind"] == ("reference" if ref_installed else "port")
+    if ref_installed:  # the reference's encoder and the numpy port are reported beside it
+        assert d["codec_config1"]["kind"] == "reference" and d["codec_config1"]["encode_mb_s"] > 0
+        assert d["port"]["value"] > 0
     e2e = d["e2e"]
     assert e2e["value"] == d["value"] and e2e["unit"] == "GB/s"
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0

@@ -136,7 +136,8 @@ class LayerPager:
     # ---- decode (experts.py:380-453) ----
 
     def decode(self, topk_ids: torch.Tensor, gather_events: list | None = None,
-               fused: bool = True, map_out: torch.Tensor | None = None) -> DecodeResult:
+               fused: bool = True, map_out: torch.Tensor | None = None,
+               decode_events: list | None = None) -> DecodeResult:
         """Page in this step's experts; returns the cache slab and expert_map.
 
         ``fused`` (default): one ``xp_decode_step`` launch does the table
@@ -144,7 +145,9 @@ class LayerPager:
         rows read (plus one decode launch when compressed).  ``fused=False``
         runs the reference's launch sequence (acquire, gather+fetch, decode,
         gather, decode).  ``gather_events``: if a list, a (start, end) pair of
-        timing events around the copying launch is appended.
+        timing events around the copying launch is appended; ``decode_events``
+        likewise around the decode launch of a compressed fused step, as
+        (start, end, rows) with rows a device scalar: the rows it expands.
 
         Host-driven callers (fused path): ``topk_ids`` may be a pinned host
         tensor (int32 or int64, contiguous), which the kernel reads through the
@@ -154,7 +157,7 @@ class LayerPager:
         run on the GPU.
         """
         if fused:
-            return self._decode_fused(topk_ids, gather_events, map_out)
+            return self._decode_fused(topk_ids, gather_events, map_out, decode_events)
         if map_out is not None:
             raise ValueError("map_out needs the fused decode step")
         store, layer = self.store, self.layer
@@ -185,7 +188,8 @@ class LayerPager:
             codec.decode_rows(ssd_todo, dst_row, cached_row, staging, self.cache_bytes, lut)
         return DecodeResult(self.cache_slab, self.expert_map)
 
-    def _decode_fused(self, topk_ids, gather_events=None, map_out=None) -> DecodeResult:
+    def _decode_fused(self, topk_ids, gather_events=None, map_out=None,
+                      decode_events=None) -> DecodeResult:
         from vllm_expert_pager import gather as gather_mod
         from vllm_expert_pager import native
         from vllm_expert_pager.table import _ids
@@ -240,8 +244,15 @@ class LayerPager:
             ev[1].record()
             gather_events.append(ev)
         if store.compress:
+            if decode_events is not None:
+                rows = (pair._vram_todo[:K] >= 0).sum()  # every VRAM miss is expanded
+                dv = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                dv[0].record()
             codec.decode_rows(pair._vram_todo[:K], pair.vram_slot, a.no_cache, staging,
                               self.cache_bytes, store.layer_lut(layer))
+            if decode_events is not None:
+                dv[1].record()
+                decode_events.append((*dv, rows))
         return DecodeResult(self.cache_slab, self.expert_map)
 
     def step_errors(self) -> int:
@@ -261,12 +272,16 @@ class LayerPager:
                                            self.layer * store.ram_slots, store.working_base)
         return cached_row, plan
 
-    def working_chunks(self, topk_ids: torch.Tensor, run_chunk, overlap: bool = True):
+    def working_chunks(self, topk_ids: torch.Tensor, run_chunk, overlap: bool = True,
+                       decode_events: list | None = None, copy_events: list | None = None):
         """Run the working path; ``run_chunk(k, n, slabs, expert_map)`` runs chunk k's MoE.
 
         With ``overlap`` chunk k+1's copies go to the other half of the working
         slab on a side stream while chunk k's MoE runs on the current stream.
-        Returns the last ``run_chunk`` result.
+        ``decode_events`` / ``copy_events``: if lists, (start, end, rows)
+        timing events around every decode / gather launch (on the copy stream)
+        are appended, rows a device scalar: the rows expanded (decode) or read
+        from the RAM tier (gather).  Returns the last ``run_chunk`` result.
         """
         store, layer = self.store, self.layer
         W = self.working.rows
@@ -286,11 +301,32 @@ class LayerPager:
                 stg = [t[h * W : (h + 1) * W].view(torch.int32) for t in staging]
             return (self.ram_view, self.cache_rows[:2], wr[:2], stg, self.scale_rows, wr[2:])
 
+        def timing(events):
+            if events is None:
+                return None
+            return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
         def copy(part, h):
+            n = None
+            if decode_events is not None or copy_events is not None:
+                # Entries not in the cache slab: read from the RAM tier, and expanded.
+                n = ((part >= 0) & (cached_row[part.clamp(min=0)] < 0)).sum()
+            ev = timing(copy_events)
+            if ev:
+                ev[0].record()
             gather_rows(part, dst_row, cached_row, src_row, 0, *rows(h))
+            if ev:
+                ev[1].record()
+                copy_events.append((*ev, n))
             if store.compress:
                 stg = [t[h * W : (h + 1) * W] for t in staging]
+                ev = timing(decode_events)
+                if ev:
+                    ev[0].record()
                 codec.decode_rows(part, dst_row, cached_row, stg, self.working_bytes[h], lut)
+                if ev:
+                    ev[1].record()
+                    decode_events.append((*ev, n))
 
         def chunk(t, k):
             return t[k * W : (k + 1) * W]
