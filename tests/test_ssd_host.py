@@ -323,3 +323,58 @@ def test_chunked_read_failure_still_writes_done(tmp_path):
             assert np.array_equal(r.row(k, 0), r.expected(k, 1, 5))
     finally:
         r.close()
+
+
+def test_pipelined_requests_finish_in_order(tmp_path):
+    """Two requests published back to back (chunk k+1's before chunk k's wait, as the
+    working path does): this server reads them with up to two in flight, and done
+    still only moves in seq order, each value after all of that request's rows landed.
+    A watcher thread records every done value it sees and checks, at that moment,
+    that the rows of every request up to it hold their records."""
+    import threading
+
+    r = Ring(native.lib(), tmp_path, L=2, E=64, R=8, working=128, workers=7,
+             pitch=(65536, 32768))
+    native.lib().ssd_set_read_chunk(ctypes.c_void_p(r.h), 16384)
+    try:
+        seen, bad = [], []
+        reqs = {}
+
+        def watch():
+            last = 0
+            t0 = time.time()
+            while last < 6 and time.time() - t0 < 20:
+                d = int(r.done[0])
+                if d != last:
+                    seen.append(d)
+                    for q in range(last + 1, d + 1):
+                        layer, experts, rows = reqs[q]
+                        for e, row in zip(experts, rows):
+                            for k in (0, 1):
+                                if not np.array_equal(r.row(k, row), r.expected(k, layer, e)):
+                                    bad.append((q, e, k))
+                    last = d
+                time.sleep(0.0001)
+
+        plan = []
+        for q in range(1, 7):
+            layer = q % 2
+            experts = list(range((q * 7) % 40, (q * 7) % 40 + 24))
+            rows = [2 * 8 + (q % 2) * 64 + i for i in range(24)]  # alternating faces
+            plan.append((layer, experts, rows))
+        th = threading.Thread(target=watch)
+        for q, (layer, experts, rows) in enumerate(plan, 1):
+            reqs[q] = (layer, experts, rows)
+        th.start()
+        # publish k+1 before waiting for k (two in flight), as the working path does
+        r.publish(*plan[0])
+        for q in range(2, 7):
+            r.publish(*plan[q - 1])
+            r.wait(q - 1)
+        r.wait(6)
+        th.join()
+        assert seen == sorted(seen) and seen[-1] == 6
+        assert not bad, bad[:5]
+        assert r.error() is None and r.stats()[:2] == (6, 6 * 24)
+    finally:
+        r.close()

@@ -14,13 +14,22 @@
 //    and honours a test-only delay.
 //
 // Implementation: one server thread spinning on the ring (a sleep adds ~100 us
-// to the round trip) and a pool of worker threads that take the request's jobs
-// one at a time under a mutex (a job is a read of hundreds of kilobytes to a
-// few megabytes).  All of them run on the CPUs of the NUMA node that holds the
-// RAM tier.  A job is one record, or, when ssd_set_read_chunk set a chunk size,
-// one page-aligned chunk of a record: a request of one or two experts then
-// keeps every reader busy instead of one or two (a disk reaches its bandwidth
-// only with several reads in flight).
+// to the round trip) and a pool of worker threads that take jobs one at a time
+// under a mutex (a job is a read of hundreds of kilobytes to a few megabytes).
+// All of them run on the CPUs of the NUMA node that holds the RAM tier.  A job
+// is one record, or, when ssd_set_read_chunk set a chunk size, one page-aligned
+// chunk of a record: a request of one or two experts then keeps every reader
+// busy instead of one or two (a disk reaches its bandwidth only with several
+// reads in flight).
+//
+// Requests are pipelined: once every job of the oldest request has been taken
+// (some may still be reading), the server admits the next published request
+// and queues its jobs behind, up to kPipeline requests in flight, so the
+// readers do not drain between consecutive requests (the working path
+// publishes chunk k+1's request before it waits for chunk k's).  done still
+// advances in seq order, each value stored only after every read of that
+// request and of the ones before it finished.  The reference serves one
+// request at a time (store.py:231-239).
 #define _GNU_SOURCE 1
 #include <errno.h>
 #include <pthread.h>
@@ -107,6 +116,8 @@ bool node_cpus(int node, cpu_set_t *set) {
   return count > 0;
 }
 
+constexpr int kPipeline = 2;  // requests in flight at once
+
 struct Server {
   int fd;
   int numa_node = -1;  // node the threads are bound to, -1 if not bound
@@ -124,14 +135,17 @@ struct Server {
   std::atomic<double> test_delay{0.0};
   std::atomic<long> read_chunk{0};  // bytes per job, 0: whole records
 
-  // the current request's jobs
-  long layer = 0;
-  std::vector<long> job_expert, job_row;
-  // Taking a job and counting it finished happen under mu, so a worker that
-  // wakes up late cannot pair an index of one request with another's count.
-  long njobs = 0, next = 0;
-  long chunk = 0, per_record = 1;  // this request's job size and jobs per record
-  std::atomic<long> finished{0};
+  // A job: bytes [lo, hi) of one record, read into that record's row; tag is
+  // the slot of its request in the ring of kPipeline requests in flight.
+  struct Job {
+    long layer, expert, row, lo, hi;
+    int tag;
+  };
+  // Jobs of the requests in flight, in admission order.  Taking a job (a copy
+  // of it) happens under mu, so appending jobs cannot race with a reader.
+  std::vector<Job> jobs;
+  long next = 0;
+  std::atomic<long> finished[kPipeline];
   std::mutex mu;
   std::condition_variable cv;
   long gen = 0;
@@ -149,12 +163,10 @@ struct Server {
     failed.store(1, std::memory_order_release);
   }
 
-  // Job j: bytes [lo, hi) of record j / per_record, lo = (j % per_record) * chunk.
   // The record is the names' pieces back to back (pitch[0] bytes of name 0,
   // then name 1, ...), each read into the row's pinned piece of that name.
-  void read_one(long j) {
-    const long r = j / per_record;
-    const long e = job_expert[r], row = job_row[r];
+  void read_one(const Job &jb) {
+    const long e = jb.expert, row = jb.row, layer = jb.layer;
     if (layer < 0 || layer >= L || e < 0 || e >= E) {
       fail("expert %ld of layer %ld is out of range", e, layer);
       return;
@@ -164,13 +176,12 @@ struct Server {
            layer, rows);
       return;
     }
-    const long lo = (j % per_record) * chunk;
-    const long hi = lo + chunk < record_bytes ? lo + chunk : record_bytes;
     iovec iov[kMaxNames];
     int k = 0;
     long base = 0;
     for (int i = 0; i < names; ++i) {
-      const long a = lo > base ? lo : base, b = hi < base + pitch[i] ? hi : base + pitch[i];
+      const long a = jb.lo > base ? jb.lo : base;
+      const long b = jb.hi < base + pitch[i] ? jb.hi : base + pitch[i];
       if (a < b) {
         iov[k].iov_base = pinned[i] + row * pitch[i] + (a - base);
         iov[k].iov_len = static_cast<size_t>(b - a);
@@ -178,27 +189,26 @@ struct Server {
       }
       base += pitch[i];
     }
-    const off_t off = static_cast<off_t>(layer * E + e) * record_bytes + lo;
+    const off_t off = static_cast<off_t>(layer * E + e) * record_bytes + jb.lo;
     ssize_t n = preadv(fd, iov, k, off);
     if (n < 0)
       fail("preadv of expert %ld of layer %ld failed: %s", e, layer, strerror(errno));
-    else if (n != hi - lo)
-      fail("short read: %zd of %ld B at byte %ld of expert %ld of layer %ld", n, hi - lo, lo, e,
-           layer);
+    else if (n != jb.hi - jb.lo)
+      fail("short read: %zd of %ld B at byte %ld of expert %ld of layer %ld", n, jb.hi - jb.lo,
+           jb.lo, e, layer);
   }
 
-  void run_jobs() {
-    for (;;) {
-      long j;
-      {
-        std::lock_guard<std::mutex> lk(mu);
-        j = next < njobs ? next++ : -1;
-      }
-      if (j < 0) return;
-      read_one(j);
+  // Takes and reads one job; false if none is waiting.
+  bool run_one() {
+    Job jb;
+    {
       std::lock_guard<std::mutex> lk(mu);
-      finished.fetch_add(1, std::memory_order_release);
+      if (next >= static_cast<long>(jobs.size())) return false;
+      jb = jobs[static_cast<size_t>(next++)];
     }
+    read_one(jb);
+    finished[jb.tag].fetch_add(1, std::memory_order_release);
+    return true;
   }
 
   void worker_main() {
@@ -210,72 +220,119 @@ struct Server {
         if (stop.load()) return;
         seen = gen;
       }
-      run_jobs();
+      while (run_one()) {
+      }
+    }
+  }
+
+  struct InFlight {
+    int64_t seq;
+    long experts, njobs;
+    double t0;
+  };
+
+  // Queues the jobs of the request in `slot` under in-flight slot `tag` and
+  // records its number of experts and jobs in f.
+  void admit(volatile int64_t *slot, int tag, InFlight &f) {
+    finished[tag].store(0, std::memory_order_relaxed);
+    std::lock_guard<std::mutex> lk(mu);
+    const long layer = static_cast<long>(slot[1]);
+    // Chunks are whole pages (O_DIRECT), and only used when the record is
+    // exactly the names' pieces (always, for records written by Store).
+    long c = read_chunk.load(std::memory_order_relaxed) / 4096 * 4096;
+    long sum = 0;
+    for (int i = 0; i < names; ++i) sum += pitch[i];
+    if (c <= 0 || c >= record_bytes || sum != record_bytes) c = record_bytes;
+    if (next >= static_cast<long>(jobs.size())) {  // every queued job taken: start afresh
+      jobs.clear();
+      next = 0;
+    }
+    long n = 0, nj = 0;
+    for (long j = 0; j < block; ++j) {
+      const int64_t e = slot[2 + j];
+      if (e < 0) continue;
+      const long row = static_cast<long>(slot[2 + block + j]);
+      for (long lo = 0; lo < record_bytes; lo += c, ++nj)
+        jobs.push_back(Job{layer, static_cast<long>(e), row, lo,
+                           lo + c < record_bytes ? lo + c : record_bytes, tag});
+      ++n;
+    }
+    f.experts = n;
+    f.njobs = nj;
+    if (nj > 1 && !workers.empty()) {  // a single job is read here without waking anyone
+      ++gen;
+      cv.notify_all();
     }
   }
 
   void server_main() {
-    int64_t last = 0, retries = 0;
+    int64_t admitted = 0, retired = 0, retries = 0;
+    InFlight fl[kPipeline];
+    int head = 0, count = 0;  // ring of in-flight requests, oldest at head
+    long spins = 0, idle = 0;
     for (;;) {
-      volatile int64_t *slot = req + kHead + ((last + 1) % ring) * slot_words;
-      long spins = 0, idle = 0;
-      int64_t seq;
-      while ((seq = load_acq(slot)) <= last) {
-        if (stop.load(std::memory_order_acquire)) return;
-        // The GPU may not have seen done: rewrite it when the re-publish count
-        // moves, or after a long idle period (store.py:200-207).
+      if (stop.load(std::memory_order_acquire)) return;
+      bool progress = false;
+      // Admit the next published request while there is room and every job of
+      // the requests in flight has been taken.
+      if (count < kPipeline) {
+        bool drained;
+        {
+          std::lock_guard<std::mutex> lk(mu);
+          drained = next >= static_cast<long>(jobs.size());
+        }
+        volatile int64_t *slot = req + kHead + ((admitted + 1) % ring) * slot_words;
+        const int64_t seq = drained || count == 0 ? load_acq(slot) : admitted;
+        if (seq > admitted) {
+          const double t0 = now_s();
+          // Requests skipped over were given up by the GPU before they arrived.
+          if (seq > admitted + 1) missed.fetch_add(static_cast<long>(seq - admitted - 1));
+          while (test_delay.load() > 0 && now_s() - t0 < test_delay.load()) {
+            if (stop.load(std::memory_order_acquire)) return;
+            usleep(1000);
+          }
+          const int tag = (head + count) % kPipeline;
+          InFlight &f = fl[tag];
+          f.seq = seq;
+          f.t0 = t0;
+          admit(slot, tag, f);
+          ++count;
+          admitted = seq;
+          progress = true;
+        }
+      }
+      // Retire the oldest request once all its reads finished: done = its seq.
+      while (count > 0) {
+        InFlight &f = fl[head];
+        if (finished[head].load(std::memory_order_acquire) < f.njobs) break;
+        fetches.fetch_add(1);
+        reads.fetch_add(f.experts);
+        io_seconds.store(io_seconds.load() + (now_s() - f.t0));
+        // Re-publishes during a long read are not lost handoffs.
+        retries = load_acq(&req[0]);
+        store_rel(done, f.seq);
+        retired = f.seq;
+        head = (head + 1) % kPipeline;
+        --count;
+        progress = true;
+      }
+      if (count > 0 && run_one()) progress = true;
+      if (progress) {
+        spins = 0;
+        idle = 0;
+        continue;
+      }
+      if (count == 0) {
+        // Idle.  The GPU may not have seen done: rewrite it when the re-publish
+        // count moves, or after a long idle period (store.py:200-207).
         int64_t r = load_acq(&req[0]);
         if (r != retries || ++idle > (1L << 25)) {
           retries = r;
           idle = 0;
-          store_rel(done, last);
-        }
-        cpu_relax(spins);
-      }
-      const double t0 = now_s();
-      // Requests skipped over were given up by the GPU before they arrived.
-      if (seq > last + 1) missed.fetch_add(static_cast<long>(seq - last - 1));
-      while (test_delay.load() > 0 && now_s() - t0 < test_delay.load()) {
-        if (stop.load(std::memory_order_acquire)) return;
-        usleep(1000);
-      }
-      long n = 0;
-      {
-        std::lock_guard<std::mutex> lk(mu);
-        layer = static_cast<long>(slot[1]);
-        for (long j = 0; j < block; ++j) {
-          int64_t e = slot[2 + j];
-          if (e < 0) continue;
-          job_expert[n] = static_cast<long>(e);
-          job_row[n] = static_cast<long>(slot[2 + block + j]);
-          ++n;
-        }
-        // Chunks are whole pages (O_DIRECT), and only used when the record is
-        // exactly the names' pieces (always, for records written by Store).
-        long c = read_chunk.load(std::memory_order_relaxed) / 4096 * 4096;
-        long sum = 0;
-        for (int i = 0; i < names; ++i) sum += pitch[i];
-        if (c <= 0 || c >= record_bytes || sum != record_bytes) c = record_bytes;
-        chunk = c;
-        per_record = (record_bytes + c - 1) / c;
-        njobs = n * per_record;
-        next = 0;
-        finished.store(0, std::memory_order_release);
-        if (njobs > 1 && !workers.empty()) {  // a single job is read here without waking anyone
-          ++gen;
-          cv.notify_all();
+          store_rel(done, retired);
         }
       }
-      run_jobs();
-      spins = 0;
-      while (finished.load(std::memory_order_acquire) < n * per_record) cpu_relax(spins);
-      fetches.fetch_add(1);
-      reads.fetch_add(n);
-      io_seconds.store(io_seconds.load() + (now_s() - t0));
-      // Re-publishes during a long read are not lost handoffs.
-      retries = load_acq(&req[0]);
-      store_rel(done, seq);
-      last = seq;
+      cpu_relax(spins);
     }
   }
 };
@@ -305,8 +362,7 @@ extern "C" void *ssd_start(int fd, void *req, void *done, long ring, long block,
     s->pitch[i] = pitch[i];
   }
   s->err[0] = 0;
-  s->job_expert.assign(static_cast<size_t>(block), 0);
-  s->job_row.assign(static_cast<size_t>(block), 0);
+  for (auto &f : s->finished) f.store(0);
   for (int i = 0; i < nworkers; ++i) s->workers.emplace_back([s] { s->worker_main(); });
   s->server = std::thread([s] { s->server_main(); });
   // The reads land in the RAM tier: run the server and its workers on the CPUs
