@@ -66,12 +66,13 @@ def parse():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--ctas", type=int, default=0, help="gather CTAs (0 = library default)")
     p.add_argument("--workload", choices=["paging", "decode", "model", "compressed", "prefill",
-                                          "reference-triton"],
+                                          "reference-triton", "links"],
                    default="paging",
                    help="paging: config 2 (the headline line); decode: the decode kernel alone; "
                         "model/compressed/prefill: configs 3/4/5 on a paged 40-layer MoE; "
                         "reference-triton: the reference's own Triton kernels from baseline/_ref "
-                        "on the inputs of paging/decode (one GPU)")
+                        "on the inputs of paging/decode (one GPU); links: every rank's "
+                        "pinned->device copy bandwidth alone and with all ranks copying")
     p.add_argument("--layers", type=int, default=40, help="MoE layers of configs 3-5")
     p.add_argument("--tokens", type=int, default=512, help="decode tokens of configs 3-4")
     p.add_argument("--c4-tokens", type=int, default=256,
@@ -217,14 +218,18 @@ def build_workload(device: torch.device):
 
 
 def measure_h2d_peak(device, world: int = 1, reps: int = 6) -> float:
-    """Copy-engine pinned->device bandwidth (GB/s), 1 GiB, best of ``reps``.
+    """Copy-engine pinned->device bandwidth (GB/s), 1 GiB, best of ``reps``, from pinned
+    memory placed on the GPU's NUMA node as the RAM tier is (xp_pinned_alloc).
 
     With several ranks every rank copies at the same time (a barrier before each
     copy), so the figure is one replica's share of the host links and host memory
     while all replicas page, which is the bench's own load.
     """
+    from vllm_expert_pager import store as store_mod
+
     n = 1 << 30
-    src = torch.empty(n, dtype=torch.uint8, pin_memory=True)
+    pinned = store_mod.PinnedBuffer(n, device, store_mod.numa_node_of(device))
+    src = pinned.cpu
     dst = torch.empty(n, dtype=torch.uint8, device=device)
     best = 0.0
     for _ in range(reps):
@@ -236,6 +241,7 @@ def measure_h2d_peak(device, world: int = 1, reps: int = 6) -> float:
         b.synchronize()
         best = max(best, n / (a.elapsed_time(b) * 1e-3) / 1e9)
     del src, dst
+    pinned.free()
     return best
 
 
@@ -830,6 +836,34 @@ def link_info(device, store, world: int, rank: int, concurrent: float) -> list[d
     out = [None] * world
     dist.all_gather_object(out, info)
     return out
+
+
+def run_links(args) -> None:
+    """--workload links: the host side of the replicas.  Every rank allocates a pinned
+    buffer on its GPU's NUMA node and measures the copy-engine pinned->device bandwidth
+    (1 GiB, best of 6) alone (ranks one after another) and with every rank copying at
+    once; rank 0 prints the per-rank figures and their sums, so that GPU subsets chosen
+    with CUDA_VISIBLE_DEVICES (two behind one PCIe switch, two behind different ones)
+    show which shared resource caps the aggregate: a switch uplink or host memory."""
+    world, rank, local = dist_setup()
+    device = torch.device("cuda", local)
+    from vllm_expert_pager import store as store_mod
+
+    class _Tier:  # what link_info reads from a Store
+        numa_node = store_mod.numa_node_of(device)
+
+    concurrent = measure_h2d_peak(device, world)
+    links = link_info(device, _Tier, world, rank, concurrent)
+    if rank == 0:
+        print(json.dumps({"workload": "links", "n_gpus": world, "links": links,
+                          "sum_idle_gb_s": round(sum(x["h2d_idle_gb_s"] for x in links), 3),
+                          "sum_concurrent_gb_s": round(sum(x["h2d_concurrent_gb_s"]
+                                                           for x in links), 3),
+                          "visible": os.environ.get("CUDA_VISIBLE_DEVICES")}), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
 
 
 def run_json_subprocess(argv: list[str], timeout: float) -> dict:
@@ -1473,6 +1507,9 @@ def main():
         return
     if args.workload in ("model", "compressed", "prefill"):
         run_model_workload(args)
+        return
+    if args.workload == "links":
+        run_links(args)
         return
     world, rank, local = dist_setup()
     if args.impl == "reference":
