@@ -202,7 +202,11 @@ int xp_set_step_wait_ns(int64_t table_ns, int64_t ssd_ns);
  * the kernel, so that a host-driven caller needs no copy-engine transfer per
  * step.  The copy CTAs wait for the others, so the launch is refused with
  * XP_ERANGE when its 2 + ctas (+1 with req) CTAs cannot all be resident on the
- * device at once. */
+ * device at once.  chunk (no counterpart in the reference, which copies whole
+ * records): with compress, the records' values per lane; then only each
+ * record's used words (its header, nibbles and Huffman words, known from the
+ * header) are copied to staging, the rest of the staging row is left as it was
+ * (the decode never reads it).  0 copies whole P-word records. */
 int xp_decode_step(const void *topk_ids, int ids_bytes, int64_t K, int64_t E,
                    int64_t *a_slot_of, int64_t *a_expert_in, int64_t *a_last_used,
                    int64_t *a_counters, int64_t a_slots, int32_t *expert_map,
@@ -214,9 +218,10 @@ int xp_decode_step(const void *topk_ids, int ids_bytes, int64_t K, int64_t E,
                    const void *src1, void *dst1, void *stg1, int64_t W1, int64_t P1,
                    const void *scale0, void *sdst0, int64_t SW0,
                    const void *scale1, void *sdst1, int64_t SW1,
-                   int compress, int ctas, int64_t layer, int64_t *seq, int64_t *req,
-                   const int64_t *done, int64_t block, int64_t ring, int64_t retry_ns,
-                   int64_t giveup, uint32_t *scratch, uint32_t *errors_out, void *stream);
+                   int compress, int64_t chunk, int ctas, int64_t layer, int64_t *seq,
+                   int64_t *req, const int64_t *done, int64_t block, int64_t ring,
+                   int64_t retry_ns, int64_t giveup, uint32_t *scratch, uint32_t *errors_out,
+                   void *stream);
 
 /* Size of the device array xp_decode_step_noalloc takes its scratch from. */
 #define XP_NOALLOC_SCRATCH_BYTES (32u << 20)

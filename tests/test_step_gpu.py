@@ -196,3 +196,41 @@ def test_step_give_ups_reach_the_host_copy_and_the_hook_check(tmp_path):
         lib.xp_set_step_wait_ns(-1, -1)
         store.test_delay(0.0)
         store.release()
+
+
+def test_compressed_step_copies_only_the_used_record_words(tmp_path):
+    """With compressed rows the fused step reads each record's used length from its
+    header and copies only those words over the host link: staging bytes past them keep
+    what was there, bytes within equal the record, and the decoded slots equal the raw
+    rows."""
+    from vllm_expert_pager import codec, synthetic
+    from vllm_expert_pager.pager import PARAMS
+
+    experts = synthetic.fp8_experts_device(E, DEV, seed=8)
+    store, pager = build(tmp_path, "t", True, 32, experts)  # every expert in RAM
+    try:
+        for t in pager.decode_staging:
+            t.fill_(0xAB)
+        ids = torch.arange(S, dtype=torch.int32, device=DEV).view(1, -1) + 3
+        res = pager.decode(ids)
+        torch.cuda.synchronize()
+        todo = pager.acquire._vram_todo[:S].cpu().tolist()
+        ram_slot = pager.acquire.ram_slot.cpu()
+        trimmed = 0
+        for k, n in enumerate(PARAMS):
+            N = store.row_bytes[n]
+            G = N // codec.GROUP
+            for j, e in enumerate(todo):
+                if e < 0:
+                    continue
+                rec = store.pinned[n][int(ram_slot[e])]
+                used = 4 * (G + 1 + N // 8 + int(rec[G]))
+                stg = pager.decode_staging[k][j].cpu()
+                assert torch.equal(stg[:used], rec.view(torch.uint8)[:used]), (n, e)
+                assert bool((stg[used:] == 0xAB).all()), (n, e)
+                trimmed += store.pitch[n] - used
+                assert torch.equal(res.slabs[n][int(res.expert_map[e])].view(torch.uint8),
+                                   experts[n][0][e].view(torch.uint8)), (n, e)
+        assert trimmed > 0
+    finally:
+        store.release()

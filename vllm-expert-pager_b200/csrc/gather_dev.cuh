@@ -54,7 +54,14 @@ struct CopyJob {
   // If set, the staging row of entry e is the position of e in stage_of[0:K]
   // instead of its position in todo (the fused step's SSD pass).
   const int64_t *stage_of;
+  // Groups per row of each name (records of 32 x chunk values per group), or 0.
+  // When set (compressed rows, at most kMaxUsed active entries), only a record's
+  // used words -- header, nibbles and Huffman words, G + 1 + W/2 + header[G] --
+  // cross the host link: the decoder never reads past them.
+  int64_t groups[2];
 };
+
+constexpr int kMaxUsed = 64;
 
 // Shared memory of copy_rows.
 struct CopySmem {
@@ -62,6 +69,7 @@ struct CopySmem {
   int64_t skip[kMaxK];
   int count;
   int warp[kThreads / 32];
+  int64_t used[kMaxUsed][2];  // words to copy of each active entry's record, per name
 };
 
 // ---- the request ring (gather.py:197-277) ----
@@ -199,6 +207,26 @@ __device__ void copy_rows(const CopyJob &a, int cta, int nctas, CopySmem &sm) {
   }
   const int64_t nact = sm.count;
   const int64_t CT = a.n[0].C + a.n[1].C;
+  // Used words of each compressed record that comes from the RAM tier: one read
+  // of its header's last entry per (entry, name), all in one round trip.
+  const bool trim = a.compress && a.groups[0] > 0 && a.groups[1] > 0 && nact <= kMaxUsed;
+  if (trim) {
+    for (int64_t t = tid; t < 2 * nact; t += kThreads) {
+      const int which = static_cast<int>(t & 1);
+      const Name &n = a.n[which];
+      const int64_t e = __ldcg(a.todo + sm.list[t >> 1]);
+      int64_t w = n.P;
+      if (__ldcg(a.cache_row + e) < 0) {
+        const int64_t G = a.groups[which];
+        const int32_t *rec = n.src + (__ldcg(a.src_row + e) + a.base) * n.P;
+        const int64_t huff = __ldcg(rec + G);
+        w = G + 1 + n.W / 2 + (huff > 0 ? huff : 0);
+        w = w < n.P ? w : n.P;
+      }
+      sm.used[t >> 1][which] = w;
+    }
+    __syncthreads();
+  }
   for (int64_t u = cta; u < nact * CT; u += nctas) {
     const int64_t j = sm.list[u / CT];
     const int64_t c = u % CT;
@@ -225,7 +253,7 @@ __device__ void copy_rows(const CopyJob &a, int cta, int nctas, CopySmem &sm) {
           if (__ldcg(a.stage_of + k) == e) srow = k;
       }
       dst = a.compress ? n.stg + srow * n.P : n.dst + dst_row * n.P;
-      len = n.P;
+      len = trim ? sm.used[u / CT][which] : n.P;
     }
     const int64_t off = piece * kPieceWords;
     if (off < len) {

@@ -110,8 +110,9 @@ extern "C" int xp_decode_step_noalloc(
                       b_last_used,
                       b_counters, b_slots, b_slot, b_todo, no_cache, base, src0, dst0, stg0, W0,
                       P0, src1, dst1, stg1, W1, P1, scale0, sdst0, SW0, scale1, sdst1, SW1,
-                      compress, ctas, layer, seq, req, done, block, ring, retry_ns, giveup,
-                      reinterpret_cast<uint32_t *>(scratch), errors_out, stream);
+                      compress, compress ? chunk : 0, ctas, layer, seq, req, done, block, ring,
+                      retry_ns, giveup, reinterpret_cast<uint32_t *>(scratch), errors_out,
+                      stream);
   if (rc != XP_OK || !compress || K == 0) return rc;
   return xp_decode_rows(a_todo, K, a_slot, no_cache, lut, stg0, P0 * 4, dst0, W0 * 4, stg1,
                         P1 * 4, dst1, W1 * 4, nullptr, chunk, stream);

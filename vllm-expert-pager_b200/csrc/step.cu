@@ -208,9 +208,9 @@ extern "C" int xp_decode_step(
     const void *src0, void *dst0, void *stg0, int64_t W0, int64_t P0,
     const void *src1, void *dst1, void *stg1, int64_t W1, int64_t P1,
     const void *scale0, void *sdst0, int64_t SW0, const void *scale1, void *sdst1, int64_t SW1,
-    int compress, int ctas, int64_t layer, int64_t *seq, int64_t *req, const int64_t *done,
-    int64_t block, int64_t ring, int64_t retry_ns, int64_t giveup, uint32_t *scratch,
-    uint32_t *errors_out, void *stream) {
+    int compress, int64_t chunk, int ctas, int64_t layer, int64_t *seq, int64_t *req,
+    const int64_t *done, int64_t block, int64_t ring, int64_t retry_ns, int64_t giveup,
+    uint32_t *scratch, uint32_t *errors_out, void *stream) {
   StepArgs p{};
   p.ids = topk_ids;
   p.ids_bytes = ids_bytes;
@@ -241,6 +241,16 @@ extern "C" int xp_decode_step(
   bool vec;
   if (!fill_names(p.ram, srcs, caches, dsts, stgs, Ws, Ps, scales, sdsts, SWs, compress, vec))
     return XP_EINVAL;
+  // Compressed rows with a known record layout: copy only each record's used words.
+  if (chunk < 0) return XP_EINVAL;
+  if (compress && chunk > 0) {
+    if (chunk % 8) return XP_EINVAL;
+    for (int i = 0; i < 2; ++i) {
+      const int64_t N = 4 * Ws[i];  // raw bytes of a row
+      if (N <= 0 || N % (32 * chunk)) return XP_EINVAL;
+      p.ram.groups[i] = N / (32 * chunk);
+    }
+  }
   p.fetch = req != nullptr;
   if (p.fetch && (!seq || !done || block < 1 || ring < 1 || K > block || retry_ns < 0 ||
                   retry_ns > XP_MAX_RETRY_NS || giveup < 0 || giveup > XP_MAX_GIVEUP))

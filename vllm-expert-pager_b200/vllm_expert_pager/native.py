@@ -51,8 +51,8 @@ _SIGNATURES = {
                               _p, _p, _p, _i64, _i64,
                               _p, _p, _p, _i64, _i64,
                               _p, _p, _i64, _p, _p, _i64,
-                              _i32, _i32, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _p,
-                              _p]),
+                              _i32, _i64, _i32, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p,
+                              _p, _p]),
     "xp_set_step_wait_ns": (_i32, [_i64, _i64]),
     "xp_decode_step_noalloc": (_i32, [_p, _i32, _i64, _i64,
                                       _p, _p, _p, _p, _i64, _p, _p, _p,

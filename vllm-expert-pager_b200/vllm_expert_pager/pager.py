@@ -232,7 +232,8 @@ class LayerPager:
                 cw[1].shape[1], self.ram_view[1].shape[1],
                 self.scale_rows[0].data_ptr(), sw[0].data_ptr(), sw[0].shape[1],
                 self.scale_rows[1].data_ptr(), sw[1].data_ptr(), sw[1].shape[1],
-                int(store.compress), gather_mod.GATHER_CTAS, layer,
+                int(store.compress), codec.CHUNK if store.compress else 0,
+                gather_mod.GATHER_CTAS, layer,
                 store.seq.data_ptr() if fetch else None, store.req_dev if fetch else None,
                 store.done_dev if fetch else None, store.block, store.ring, store.retry_ns,
                 store.giveup, self.step_scratch.data_ptr(), self.step_errors_host.data_ptr(),
