@@ -582,6 +582,9 @@ def model_decode(m, device, batch: int, tokens: int, h2d_peak: float | None = No
     del graph
     m.check()
     record = store.record_bytes if store.compress else EXPERT_BYTES
+    # The fused step copies a compressed record's used words only (its header says
+    # how many); the working path's gather copies whole records.
+    step_bytes = m.used_mean if store.compress else EXPERT_BYTES
     res = {"layers": m.L, "batch": batch, "tokens": tokens, "ms": round(ms, 2),
            "tok_per_s": round(tokens * batch / (ms * 1e-3), 2),
            "tpot_ms": round(ms / tokens, 3),
@@ -593,7 +596,8 @@ def model_decode(m, device, batch: int, tokens: int, h2d_peak: float | None = No
            "step_errors": sum(p.step_errors() for p in m.pagers),
            "clocks": clocks.summary(), "finite": finite}
     if batch * TOPK <= m.S:
-        res["paged_gb_per_s"] = round(misses * record / (ms * 1e-3) / 1e9, 3)
+        res["paged_gb_per_s"] = round(misses * step_bytes / (ms * 1e-3) / 1e9, 3)
+        res["paged_bytes_per_miss"] = int(step_bytes)
         res["vram_misses_per_layer_step"] = round(misses / (tokens * m.L), 3)
 
     # Probe: the same steps eagerly, with events around every paging launch.
@@ -633,11 +637,12 @@ def model_decode(m, device, batch: int, tokens: int, h2d_peak: float | None = No
                 "bound": "host_link", "launches": len(t_all),
                 "launches_with_ssd": sum(1 for _, ssd in steps if ssd), "unit": "GB/s"}
         if ram:
-            b_ = sum(n for _, n in ram) * record
+            b_ = sum(n for _, n in ram) * step_bytes
             ach = b_ / (sum(ms_ for ms_, _ in ram) * 1e-3) / 1e9
             link.update({"achieved": round(ach, 3),
-                         "how": "steps served from the RAM tier alone: record bytes of "
-                                "their misses / their step-kernel time"})
+                         "how": "steps served from the RAM tier alone: bytes copied for "
+                                "their misses (compressed: the records' used bytes, mean over "
+                                "the pool) / their step-kernel time"})
             if h2d_peak:
                 link.update({"peak": round(h2d_peak, 3), "frac": round(ach / h2d_peak, 4)})
         probe_res["host_link"] = link
