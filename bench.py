@@ -23,7 +23,9 @@ RAM over the host link (+ the SSD-fetch CTA, idle here).
              40-layer paged MoE with the compressed RAM tier (R=128) and the
              O_DIRECT paging file at batch 1 and 8 under CUDA graphs, each with
              the in-run host-link roofline of its copy kernel, the in-run HBM
-             roofline of the decode kernel and the SSD rate vs the disk's peak
+             roofline of the decode kernel and the SSD rate vs the disk's peak;
+             and config 5, the chunked 2048-token prefill (8 layers) on the SSD
+             tier and on a RAM-resident compressed tier, overlapped and serial
   kernels  = decode / acquire / encode kernels alone, and the reference's own
              Triton kernels on the same inputs (a subprocess)
   cpu_baseline = the reference's own CPU code (its ExpertTable on CPU tensors +
@@ -78,9 +80,11 @@ def parse():
     p.add_argument("--c4-tokens", type=int, default=256,
                    help="batch-1 decode tokens of the default line's config-4 entries "
                         "(batch 8 runs a quarter as many steps)")
+    p.add_argument("--c5-layers", type=int, default=8,
+                   help="layers of the default line's config-5 prefill entry")
     p.add_argument("--skip", default="",
                    help="comma-separated parts of the default line to leave out: "
-                        "compressed, reference_triton, cpu, kernels")
+                        "compressed, prefill, reference_triton, cpu, kernels")
     return p.parse_args()
 
 
@@ -683,16 +687,17 @@ def run_prefill(args, device, path) -> dict:
     out = {}
     for tier, R_, p_ in (("ssd", 128, path), ("ram", E, None)):
         res = {}
+        # One model per tier: its working slab has two halves; the serial run uses one.
+        m = PagedMoE(device, layers=args.layers, S=S, R=R_, compress=True, path=p_,
+                     overlap=True)
+        gen = torch.Generator(device=device).manual_seed(13)
+        T = 2048
+        h = (torch.randn((T, 2048), generator=gen, device=device) * 0.5).to(torch.bfloat16)
+        ids = synthetic.uniform_routing(T, seed=5).to(device)
+        w = torch.softmax(torch.randn((T, TOPK), generator=gen, device=device), -1)
+        cfg = m.config(T)
+        moe = m.moe
         for overlap in (True, False):
-            m = PagedMoE(device, layers=args.layers, S=S, R=R_, compress=True, path=p_,
-                         overlap=overlap)
-            gen = torch.Generator(device=device).manual_seed(13)
-            T = 2048
-            h = (torch.randn((T, 2048), generator=gen, device=device) * 0.5).to(torch.bfloat16)
-            ids = synthetic.uniform_routing(T, seed=5).to(device)
-            w = torch.softmax(torch.randn((T, TOPK), generator=gen, device=device), -1)
-            cfg = m.config(T)
-            moe = m.moe
 
             def layer_paged(l):
                 acc = {}
@@ -712,7 +717,8 @@ def run_prefill(args, device, path) -> dict:
             layer_paged(0)  # warm-up (JIT)
             torch.cuda.synchronize()
             reads0 = m.store.reads
-            ms = timed(lambda: [layer_paged(l) for l in range(args.layers)])
+            with Clocks(torch.cuda.current_device()) as clocks:
+                ms = timed(lambda: [layer_paged(l) for l in range(args.layers)])
             reads = m.store.reads - reads0
             # MoE alone on resident weights (the pool), for the overlap fraction.
             pw = m.pool_weights
@@ -724,11 +730,13 @@ def run_prefill(args, device, path) -> dict:
             res["overlap" if overlap else "serial"] = {
                 "ms_per_layer": round(ms / args.layers, 3), "ssd_reads": reads,
                 "ssd_gb_per_s": round(reads * m.store.record_bytes / (ms * 1e-3) / 1e9, 3),
-                "moe_only_ms_per_layer": round(moe_ms / args.layers, 3)}
-            m.release()
+                "moe_only_ms_per_layer": round(moe_ms / args.layers, 3),
+                "clocks": clocks.summary()}
+        res["giveups"] = int(m.store.req[m.store.giveup_at])
+        res["ssd_failed"] = m.store.failed
+        m.release()
         o, s_ = res["overlap"]["ms_per_layer"], res["serial"]["ms_per_layer"]
         moe_ms = res["serial"]["moe_only_ms_per_layer"]
-        # Of the MoE's time, the share the overlapped run hid under the copies.
         res["hidden_fraction_of_moe"] = round(max(0.0, min(1.0, (s_ - o) / max(moe_ms, 1e-9))), 3)
         res["tier"] = (f"R={R_} compressed" + (" + O_DIRECT paging file" if p_ else
                                                 ", every record in pinned RAM, no SSD"))
@@ -816,6 +824,39 @@ def compressed_configs(args, device, h2d_peak: float) -> dict:
             m.release()
         if os.path.exists(path):
             os.unlink(path)
+    return out
+
+
+def prefill_configs(args, device) -> dict:
+    """Config 5 in the default line: the 2048-token prefill through ``--c5-layers`` layers
+    on the compressed SSD tier (R=128 + paging file) and on a RAM-resident compressed tier
+    (R=E), each with chunk k+1's copies overlapped with chunk k's MoE and serial, with the
+    SSD rate against the disk's own peak."""
+    import copy as _copy
+
+    base = os.environ.get("XP_BENCH_DIR", "/tmp")
+    path = os.path.join(base, f"xpager_bench_c5_{os.getpid()}.bin")
+    a = _copy.copy(args)
+    a.layers = args.c5_layers
+    try:
+        out = run_prefill(a, device, path)
+        if os.path.exists(path):
+            from vllm_expert_pager.codec import pitch_of
+            from vllm_expert_pager import synthetic
+
+            record = sum(pitch_of(r * c, 0.89, 4096) for r, c in synthetic.SHAPES.values())
+            peak = disk_peak(path, record)
+            out["disk_peak"] = peak
+            if "gb_per_s" in peak:
+                for mode in ("overlap", "serial"):
+                    v = out["ssd"][mode]
+                    v["ssd_frac_of_disk_peak"] = round(v["ssd_gb_per_s"] / peak["gb_per_s"], 3)
+    finally:
+        if os.path.exists(path):
+            os.unlink(path)
+    out["layers"] = a.layers
+    out["workload"] = ("2048-token prefill, uniform top-8 over E=256, CACHE_SLOTS=32, "
+                       "WORKING_ROWS=64 (5 chunks per layer), the 40-layer model's layers")
     return out
 
 
@@ -1649,6 +1690,15 @@ def main():
         store = None
         torch.cuda.empty_cache()
         configs = compressed_configs(args, device, peak)
+    if world == 1 and "prefill" not in skip:
+        if configs is None:
+            configs = {}
+            if store is not None:
+                del pager, trace, host_trace
+                store.release()
+                store = None
+                torch.cuda.empty_cache()
+        configs["prefill_config5"] = prefill_configs(args, device)
 
     if rank == 0:
         steps_total = args.steps * W
