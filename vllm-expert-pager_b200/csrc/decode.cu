@@ -169,9 +169,14 @@ constexpr size_t kRingSmem = kWarps * kRing + kRing;
 // at i+1 (the refill leaves at least 23 bits after symbol i), so each lane
 // refills at most once per pair, at i (level < 9) or at i+1 (level >= 9 and
 // level - len_i < 9, len_i from a length-only lookup of the current buffer,
-// which holds level >= 9 valid bits).  Two ballots order the pair's refills as
-// the format does (all of symbol i's in lane order, then symbol i+1's), one
-// shared load gives each refilling lane its word, and the word is inserted
+// which holds level >= 9 valid bits).  The pair's refills go in the format's
+// order (all of symbol i's in lane order, then symbol i+1's): with C0 the
+// ballot of lanes refilling at i and C1 that of lanes refilling at i or i+1
+// (level + len_i < 9 + len_i, i.e. nv + len_i >= 0, which holds for every lane
+// refilling at i as well), a lane refilling at slot k takes the word after
+// popc(C_{k-1} | (C_k & lanes below it)) others (C_{-1} = 0), and the pair uses
+// popc(C1) words; one shared load gives each refilling lane its word, and the
+// word is inserted
 // right above the lane's valid bits before symbol i: for a lane refilling at
 // i+1 that is where the format puts it after symbol i's bits are consumed, and
 // symbol i reads only bits below it.  The insert position is at most 23 bits,
@@ -182,7 +187,7 @@ __device__ __forceinline__ void step_pair(uint64_t &buf, int &nv, uint32_t &off,
                                           uint32_t &e0, uint32_t &e1) {
   asm volatile(
       "{\n\t"
-      ".reg .pred p0, p1, ev;\n\t"
+      ".reg .pred p0, ev;\n\t"
       ".reg .b32 x, ia, l0, t, b0, b1, n0, n1, mb, c, a, w, m, len;\n\t"
       "setp.ge.s32 p0, %1, 0;\n\t"
       "cvt.u32.u64 x, %0;\n\t"
@@ -190,22 +195,19 @@ __device__ __forceinline__ void step_pair(uint64_t &buf, int &nv, uint32_t &off,
       "or.b32 ia, ia, %8;\n\t"
       "ld.shared.u8 l0, [ia];\n\t"
       "add.s32 t, %1, l0;\n\t"
-      "setp.ge.and.s32 p1, t, 0, !p0;\n\t"
+      "setp.ge.s32 ev, t, 0;\n\t"
       "vote.sync.ballot.b32 b0, p0, 0xffffffff;\n\t"
-      "vote.sync.ballot.b32 b1, p1, 0xffffffff;\n\t"
-      "popc.b32 n0, b0;\n\t"
+      "vote.sync.ballot.b32 b1, ev, 0xffffffff;\n\t"
+      "selp.b32 n0, 0, b0, p0;\n\t"
       "selp.b32 mb, b0, b1, p0;\n\t"
-      "and.b32 mb, mb, %5;\n\t"
+      "lop3.b32 mb, mb, n0, %5, 0xE4;\n\t"
       "popc.b32 c, mb;\n\t"
-      "@!p0 add.s32 c, c, n0;\n\t"
       "mad.lo.u32 a, c, 4, %2;\n\t"
       "and.b32 a, a, " XP_RING_MASK ";\n\t"
       "or.b32 a, a, %6;\n\t"
       "ld.shared.u32 w, [a];\n\t"
       "popc.b32 n1, b1;\n\t"
-      "add.s32 n1, n1, n0;\n\t"
       "mad.lo.u32 %2, n1, 4, %2;\n\t"
-      "or.pred ev, p0, p1;\n\t"
       "add.s32 t, %1, 15;\n\t"
       "shr.b32 m, 8388608, t;\n\t"
       "@ev mad.wide.u32 %0, w, m, %0;\n\t"
@@ -235,8 +237,11 @@ __device__ __forceinline__ void step_pair(uint64_t &buf, int &nv, uint32_t &off,
 // most once in three consecutive symbols.  Its refill symbol k (level < 9 before
 // symbol k, the earlier symbols' lengths from two chained length-only lookups
 // of the current buffer) is known before any of the three is decoded; three
-// ballots order the refills as the format does (symbol i's refilling lanes in
-// lane order, then i+1's, then i+2's) and the word goes in right above the
+// cumulative ballots (refills at a slot <= 0, <= 1, <= 2; as in step_pair each
+// follows from one comparison, nv + len_i + ... >= 0) order the refills as the
+// format does (symbol i's refilling lanes in lane order, then i+1's, then
+// i+2's), each lane's word index from one popc as in step_pair, and the word
+// goes in right above the
 // lane's valid bits before symbol i, at most 26 bits up (level < 9 + two codes
 // of at most 9 bits), where the 64-bit buffer holds it; its multiplier
 // 0x4000000 >> (nv + 18) is 1 << level for level <= 26.
@@ -245,8 +250,8 @@ __device__ __forceinline__ void step_triple(uint64_t &buf, int &nv, uint32_t &of
                                             uint32_t &e0, uint32_t &e1, uint32_t &e2) {
   asm volatile(
       "{\n\t"
-      ".reg .pred p0, p1, p2, q, ev;\n\t"
-      ".reg .b32 x, lo, hi, l0, l1, t, b0, b1, b2, n0, n1, s01, mb, c, bs, a, w, m, len;\n\t"
+      ".reg .pred p0, q, ev;\n\t"
+      ".reg .b32 x, lo, hi, l0, l1, t, b0, b1, b2, n1, mb, c, bs, a, w, m, len;\n\t"
       "setp.ge.s32 p0, %1, 0;\n\t"
       "mov.b64 {lo, hi}, %0;\n\t"
       "and.b32 x, lo, 511;\n\t"
@@ -257,31 +262,24 @@ __device__ __forceinline__ void step_triple(uint64_t &buf, int &nv, uint32_t &of
       "or.b32 x, x, %9;\n\t"
       "ld.shared.u8 l1, [x];\n\t"
       "add.s32 t, %1, l0;\n\t"
-      "setp.ge.and.s32 p1, t, 0, !p0;\n\t"
-      "or.pred q, p0, p1;\n\t"
+      "setp.ge.s32 q, t, 0;\n\t"
       "add.s32 t, t, l1;\n\t"
-      "setp.ge.and.s32 p2, t, 0, !q;\n\t"
+      "setp.ge.s32 ev, t, 0;\n\t"
       "vote.sync.ballot.b32 b0, p0, 0xffffffff;\n\t"
-      "vote.sync.ballot.b32 b1, p1, 0xffffffff;\n\t"
-      "vote.sync.ballot.b32 b2, p2, 0xffffffff;\n\t"
-      "popc.b32 n0, b0;\n\t"
-      "popc.b32 n1, b1;\n\t"
-      "add.s32 s01, n0, n1;\n\t"
-      "selp.b32 mb, b1, b2, p1;\n\t"
-      "selp.b32 mb, b0, mb, p0;\n\t"
-      "selp.b32 bs, n0, s01, p1;\n\t"
-      "selp.b32 bs, 0, bs, p0;\n\t"
-      "and.b32 mb, mb, %6;\n\t"
+      "vote.sync.ballot.b32 b1, q, 0xffffffff;\n\t"
+      "vote.sync.ballot.b32 b2, ev, 0xffffffff;\n\t"
+      "selp.b32 mb, b0, b1, q;\n\t"
+      "selp.b32 mb, 0, mb, p0;\n\t"
+      "selp.b32 bs, b1, b2, q;\n\t"
+      "selp.b32 bs, b0, bs, p0;\n\t"
+      "lop3.b32 mb, bs, mb, %6, 0xE4;\n\t"
       "popc.b32 c, mb;\n\t"
-      "add.s32 c, c, bs;\n\t"
       "mad.lo.u32 a, c, 4, %2;\n\t"
       "and.b32 a, a, " XP_RING_MASK ";\n\t"
       "or.b32 a, a, %7;\n\t"
       "ld.shared.u32 w, [a];\n\t"
       "popc.b32 n1, b2;\n\t"
-      "add.s32 n1, n1, s01;\n\t"
       "mad.lo.u32 %2, n1, 4, %2;\n\t"
-      "or.pred ev, q, p2;\n\t"
       "add.s32 t, %1, 18;\n\t"
       "shr.b32 m, 67108864, t;\n\t"
       "@ev mad.wide.u32 %0, w, m, %0;\n\t"
