@@ -1,26 +1,35 @@
-"""The refill schedule of the GPU decoder (decode.cu), modelled on the CPU.
+"""The GPU decoder's round schedule and bit arithmetic (decode.cu), modelled on the CPU.
 
 The record format (monochromegane/vllm-expert-pager src/vllm_expert_pager/codec.py:
 22-26, 204-245) refills a lane's bit buffer with one 32-bit word before every
 symbol at which it holds fewer than 9 bits, the lanes refilling at the same
 symbol taking consecutive words in lane order.  decode_ring_kernel does not
 follow that schedule literally: it decodes 8 symbols in rounds of 3, 3 and 2
-symbols (step_triple, step_pair) and, per round,
+symbols (round3, round2) and, per round,
 
 * finds the one symbol of the round at which each lane refills, if any, from
-  its current buffer alone (a lane refills at most once in three consecutive
-  symbols, and before a symbol it does not refill at it holds >= 9 valid bits,
-  enough to look up that symbol's length);
+  table entries looked up in its current buffer (a lane refills at most once in
+  three consecutive symbols, and before a symbol it does not refill at it holds
+  >= 9 valid bits, so that symbol's entry is exact);
 * gives the round's refilling lanes their words in the format's order (the
-  first symbol's refilling lanes in lane order, then the second's, ...);
+  first symbol's refilling lanes in lane order, then the second's, ...), from
+  three cumulative ballots and one popcount per lane;
 * inserts each word right above the lane's valid bits before the round's
-  first symbol, at most 26 bits up, so a 64-bit buffer holds it.
+  first symbol (at most bit 27: the buffer keeps stream bit j at bit j + 1);
+* looks windows up with as many bits as the row's longest code;
+* decodes the round's symbols from the new buffer with wrapping funnel shifts
+  whose amount is the 16-bit table entry len | sym << 12 itself, re-looking up
+  the first two symbols only in lanes whose refill came at or before them;
+* keeps the level as (26 - level) << 25, updated by entry x 2^25 multiply-adds;
+* packs the exponent fields of 4 symbols with multiplies (e >> 9, e >> 1,
+  e << 7, e << 15) and merges the sign/mantissa nibbles by a byte permute.
 
-This test runs that schedule on the CPU (one lane at a time, no GPU) and checks
-that it decodes the reference's golden records and records of other exponent
-distributions byte for byte like the sequential decoder of the CPU oracle, and
-that the insert position bound holds.  It pins the algorithm; the GPU tests pin
-the kernel.
+This test runs that arithmetic on the CPU, 32-bit op for op (numpy, one array
+element per lane, no GPU), and checks that it decodes the reference's golden
+records and records of other exponent distributions byte for byte like the
+sequential decoder of the CPU oracle, and that the insert position and level
+counter stay in the ranges the kernel relies on.  It pins the algorithm; the GPU
+tests pin the kernel.
 """
 
 import numpy as np
@@ -29,56 +38,108 @@ import pytest
 from oracle import codec as oc
 
 GOLDEN = np.load(__file__.rsplit("/", 1)[0] + "/golden/codec.npz")
-ROUNDS = (3, 3, 2)  # symbols per ballot round within each 8 symbols
-LANES, LIMIT = 32, 9
+LANES = 32
+M32 = 0xFFFFFFFF
+LT = np.array([(1 << lane) - 1 for lane in range(LANES)], np.uint64)
+NV_START, NV_REFILL = 26 << 25, 18 << 25
+
+
+def _s32(x):
+    x = np.asarray(x, np.int64) & M32
+    return np.where(x >= 1 << 31, x - (1 << 32), x)
+
+
+def _shf_r_wrap(lo, hi, c):
+    """PTX shf.r.wrap.b32: low word of (hi:lo) >> (c & 31)."""
+    v = (hi.astype(np.uint64) << 32) | lo.astype(np.uint64)
+    return ((v >> (c.astype(np.uint64) & 31)) & M32).astype(np.uint64)
+
+
+def _ballot(pred):
+    return int(sum(1 << i for i in np.nonzero(pred)[0]))
+
+
+def _popc(x):
+    return np.array([bin(int(v)).count("1") for v in x], np.uint64)
+
+
+def _table(lut):
+    lut = lut.astype(np.uint64)
+    return (lut & 15) | ((lut >> 4) << 12)
 
 
 def decode_rounds(rec: np.ndarray, lut: np.ndarray, n: int, chunk: int) -> np.ndarray:
     G = n // (chunk * LANES)
-    i32 = rec[: (len(rec) // 4) * 4].view(np.uint32)
+    i32 = rec[: (len(rec) // 4) * 4].view(np.uint32).astype(np.uint64)
     nib_w, huff_w = G + 1, (4 * (G + 1) + n // 2) // 4
-    ent_of = [int(x) for x in lut]
+    T = _table(lut)
+    # windows are looked up with as many bits as the row's longest code
+    msk = ((1 << int((lut & 15).max())) - 1) << 1
+    look = lambda x: T[(x & msk) >> 1]  # noqa: E731  (the table byte address is x & msk)
     out = np.zeros(n, np.uint8)
+    zero = np.zeros(LANES, np.uint64)
     for g in range(G):
         off = int(i32[g])
-        buf, lvl = [0] * LANES, [0] * LANES
-        i, r = 0, 0
-        while i < chunk:
-            D = ROUNDS[r % len(ROUNDS)]
-            r += 1
-            # the round's refill symbol of each lane, from its current bits only
-            at = [None] * LANES
-            for lane in range(LANES):
-                level, b = lvl[lane], buf[lane]
-                for k in range(D):
-                    if level < LIMIT:
-                        at[lane] = k
-                        break
-                    ln = ent_of[b & 511] & 15
-                    level, b = level - ln, b >> ln
-            count = [at.count(k) for k in range(D)]
-            taken = [0] * D
-            for lane in range(LANES):
-                k = at[lane]
-                if k is None:
-                    continue
-                rank = sum(count[:k]) + taken[k]
-                taken[k] += 1
-                assert lvl[lane] <= 26, "insert position above 26 bits"
-                buf[lane] |= int(i32[huff_w + off + rank]) << lvl[lane]
-                lvl[lane] += 32
-                assert lvl[lane] <= 64
-            off += sum(count)
-            for k in range(D):
-                for lane in range(LANES):
-                    e = ent_of[buf[lane] & 511]
-                    buf[lane] >>= e & 15
-                    lvl[lane] -= e & 15
-                    v = i + k
-                    nib = int(i32[nib_w + (g * (chunk // 8) + v // 8) * LANES + lane])
-                    s = (nib >> (4 * (v % 8))) & 15
-                    out[(g * LANES + lane) * chunk + v] = ((s & 8) << 4) | ((e >> 4) << 3) | (s & 7)
-            i += D
+        lo, hi = zero.copy(), zero.copy()
+        nv = np.full(LANES, NV_START, np.int64)
+        for m in range(chunk // 8):
+            ents = []
+            for size in (3, 3, 2):
+                e0 = look(lo)
+                t1 = _s32(nv + (e0.astype(np.int64) << 25))
+                p0, q = nv >= NV_REFILL, t1 >= NV_REFILL
+                if size == 3:
+                    e1 = look(_shf_r_wrap(lo, hi, e0))
+                    ev = _s32(t1 + (e1.astype(np.int64) << 25)) >= NV_REFILL
+                    b0, b1, b2 = _ballot(p0), _ballot(q), _ballot(ev)
+                    bs = np.where(p0, b0, np.where(q, b1, b2)).astype(np.uint64)
+                    mb = np.where(p0, 0, np.where(q, b0, b1)).astype(np.uint64)
+                else:
+                    ev = q
+                    b0, b2 = _ballot(p0), _ballot(ev)
+                    bs = np.where(p0, b0, b2).astype(np.uint64)
+                    mb = np.where(p0, 0, b0).astype(np.uint64)
+                rank = _popc((bs & LT) | (mb & ~LT & M32))
+                word = i32[huff_w + off + rank.astype(np.int64)]
+                off += bin(b2).count("1")
+                s = (nv.astype(np.uint64) & M32) >> 25
+                assert np.all(s[ev] <= 26), "insert above bit 27"
+                mul = np.where(s < 32, (1 << 27) >> np.minimum(s, 31), 0).astype(np.uint64)
+                old = (hi << 32) | lo
+                assert np.all(old[ev] < mul[ev]), "bits at or above the insert position"
+                buf = old + np.where(ev, word * mul, 0)
+                lo, hi = buf & M32, buf >> 32
+                nv = np.where(ev, nv - (32 << 25), nv)
+                # decode from the new buffer; the first entries again only where stale
+                d0 = np.where(p0, look(lo), e0)
+                x = _shf_r_wrap(lo, hi, d0)
+                if size == 3:
+                    d1 = np.where(q, look(x), e1)
+                    x = _shf_r_wrap(x, zero, d1)
+                    d = [d0, d1, look(x)]
+                else:
+                    d = [d0, look(x)]
+                sh = sum(d) & M32
+                lo, hi = _shf_r_wrap(lo, hi, sh), _shf_r_wrap(hi, zero, sh)
+                nv = _s32(nv + (sh.astype(np.int64) << 25))
+                assert np.all((nv >= -32 << 25) & (nv <= NV_START)), "level out of range"
+                ents += d
+            mulhi = lambda a, b: (a * b) >> 32  # noqa: E731
+            words = []
+            for h in range(2):
+                e = ents[4 * h: 4 * h + 4]
+                acc = (mulhi(e[0], 1 << 23) + mulhi(e[1], 1 << 31) + (e[2] << 7) + (e[3] << 15)) & M32
+                words.append(acc)
+            nw = i32[nib_w + (g * (chunk // 8) + m) * LANES + np.arange(LANES)]
+            ev_ = ((nw & 0x0F0F0F0F) * 17) & M32
+            od_ = ((((nw * (1 << 28)) >> 32) & 0x0F0F0F0F) * 17) & M32
+            for h, sel in enumerate(((0, 4, 1, 5), (2, 6, 3, 7))):
+                src = (od_ << 32) | ev_
+                t = sum(((src >> (8 * b)) & 0xFF) << (8 * i) for i, b in enumerate(sel))
+                w = (words[h] & 0x78787878) | (t & ~np.uint64(0x78787878) & M32)
+                for k in range(4):
+                    pos = (g * LANES + np.arange(LANES)) * chunk + 8 * m + 4 * h + k
+                    out[pos] = (w >> (8 * k)) & 0xFF
         assert off <= int(i32[g + 1]), "read past the group's words"
     return out
 

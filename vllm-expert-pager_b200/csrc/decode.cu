@@ -17,20 +17,24 @@
 //    read consecutive words (ballot + popc give each its slot), one
 //    conflict-free shared load.  The ring (instead of staging a whole group,
 //    ~7.3 KiB) and a 48-register bound let 10 CTAs (40 warps) share an SM.
-//  * Several symbols per ballot round (step_triple, step_pair; 8 symbols in
-//    rounds of 3 + 3 + 2): a lane refills at most once in three consecutive
-//    symbols, its refill symbol follows from length-only lookups of its current
-//    buffer, and its word can be inserted above its valid bits before the
-//    round's first symbol; so one round of ballots and one word load serves
-//    two or three symbols, which cuts the refill work on the symbol-to-symbol
-//    chain.
-//  * One lookup in the 512-byte LUT per symbol (the table is 512-byte aligned,
-//    so its address is one AND/OR of the window).
-//  * Every instruction is integer work; the integer ALU pipe (one warp
-//    instruction per two cycles per scheduler) is the busiest unit in large
-//    launches.  Exponent bits of 4 symbols are summed with multiply-adds and
-//    sign/mantissa nibbles spread with multiplies, both on the FMA pipe; one
-//    select merges them.
+//  * Several symbols per ballot round (round3, round2; 8 symbols in rounds of
+//    3 + 3 + 2): a lane refills at most once in three consecutive symbols, its
+//    refill symbol follows from table lookups in its current buffer, and its
+//    word can be inserted above its valid bits before the round's first
+//    symbol; so one round of ballots and one word load serves two or three
+//    symbols.  Only the lanes whose refill came at or before one of the
+//    round's first two symbols look that symbol up again (predicated loads).
+//  * Position-based symbol chain: a per-warp table of 16-bit entries
+//    len | sym << 12 whose low five bits are the code length, the stream kept
+//    one bit up in a 64-bit register pair so a window's table address is one
+//    AND/OR; each next window is one wrapping funnel shift by the previous
+//    entry, and the buffer is shifted once per round by the sum of the
+//    round's entries.  Per symbol: address, load, funnel shift.
+//  * The level counter sits in the top seven bits of a register, so every
+//    length update is an entry x 2^25 multiply-add on the FMA pipe; the
+//    exponent fields are packed by multiplies too, and the sign/mantissa
+//    nibbles spread by multiplies and one byte permute.  The integer ALU pipe
+//    (one warp instruction per two cycles per scheduler) takes the rest.
 //  * Each lane stores 16 bytes per 16 symbols; nibble words are loaded two
 //    iterations ahead and prefetched into L2 eight iterations ahead.
 #include "common.cuh"
@@ -66,7 +70,7 @@ struct DecodeArgs {
 // slid with coalesced loads, words handed out by shuffles.
 __device__ void decode_group_window(const uint32_t *huff, int64_t wbase, int64_t rend,
                                     const uint32_t *nib, uint8_t *out_row, int64_t chunk,
-                                    const uint8_t *L, int lane) {
+                                    const uint16_t *T, int lane) {
   auto ld = [&](int64_t idx) -> uint32_t {
     return (idx >= 0 && idx < rend) ? __ldg(huff + idx) : 0u;
   };
@@ -99,12 +103,12 @@ __device__ void decode_group_window(const uint32_t *huff, int64_t wbase, int64_t
           w2 = ld(wbase + 64 + lane);
         }
       }
-      const uint32_t ent = L[buf & (kLutBytes - 1)];
+      const uint32_t ent = T[buf & (kLutBytes - 1)];  // len | sym << 12
       const uint32_t len = ent & 15;
       buf >>= len;
       level -= static_cast<int>(len);
       const uint32_t s = (nw >> (4 * k)) & 15;
-      const uint32_t byte = ((s & 8) << 4) | ((ent >> 4) << 3) | (s & 7);
+      const uint32_t byte = ((s & 8) << 4) | ((ent >> 12) << 3) | (s & 7);
       if (k < 4) lo |= byte << (8 * k);
       else hi |= byte << (8 * (k - 4));
     }
@@ -125,24 +129,21 @@ __device__ __forceinline__ uint32_t mul_u32(uint32_t a, uint32_t b) {
   asm("mul.lo.u32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
   return d;
 }
+__device__ __forceinline__ uint32_t mulhi_u32(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.hi.u32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t madhi_u32(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("mad.hi.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
 // Bitwise select: (a & m) | (b & ~m), one three-input logic op.
 __device__ __forceinline__ uint32_t bitsel(uint32_t a, uint32_t b, uint32_t m) {
   uint32_t d;
   asm("lop3.b32 %0, %1, %2, %3, 0xE4;" : "=r"(d) : "r"(a), "r"(b), "r"(m));
   return d;
-}
-
-// Output bytes of 4 symbols: acc = e0 + e1 << 8 + e2 << 16 + e3 << 24 (LUT
-// entries sym << 4 | len), x = their 4 sign/mantissa nibbles (bits 0..15).
-// Byte k = (s & 8) << 4 | sym << 3 | (s & 7).  The nibbles are spread to one
-// per byte with two multiplies whose partial products do not collide inside
-// the kept bits (x & 0x0F0F times 257 puts n0, n2 at bytes 0, 2; x & 0xF0F0
-// times 4112 puts n1, n3 at bytes 1, 3), t * 17 copies each nibble to the high
-// half of its byte, and one select merges the exponent field (acc >> 1 has
-// sym at bits 3..6 of each byte) with the sign and mantissa bits.
-__device__ __forceinline__ uint32_t merge4(uint32_t acc, uint32_t x) {
-  const uint32_t t = bitsel(mul_u32(x & 0x0F0Fu, 257u), mul_u32(x & 0xF0F0u, 4112u), 0x001F001Fu);
-  return bitsel(acc >> 1, mul_u32(t, 17u), 0x78787878u);
 }
 
 // Word ring.  Each warp streams its group's Huffman words through a 2 KiB
@@ -165,149 +166,155 @@ constexpr uint32_t kMaxAdvance = 6 * 32 * 4;
 // Dynamic shared memory per CTA: kWarps rings plus the slack that aligns them.
 constexpr size_t kRingSmem = kWarps * kRing + kRing;
 
-// Two symbols per ballot round.  A lane that refills at symbol i cannot refill
-// at i+1 (the refill leaves at least 23 bits after symbol i), so each lane
-// refills at most once per pair, at i (level < 9) or at i+1 (level >= 9 and
-// level - len_i < 9, len_i from a length-only lookup of the current buffer,
-// which holds level >= 9 valid bits).  The pair's refills go in the format's
-// order (all of symbol i's in lane order, then symbol i+1's): with C0 the
-// ballot of lanes refilling at i and C1 that of lanes refilling at i or i+1
-// (level + len_i < 9 + len_i, i.e. nv + len_i >= 0, which holds for every lane
-// refilling at i as well), a lane refilling at slot k takes the word after
-// popc(C_{k-1} | (C_k & lanes below it)) others (C_{-1} = 0), and the pair uses
-// popc(C1) words; one shared load gives each refilling lane its word, and the
-// word is inserted
-// right above the lane's valid bits before symbol i: for a lane refilling at
-// i+1 that is where the format puts it after symbol i's bits are consumed, and
-// symbol i reads only bits below it.  The insert position is at most 23 bits,
-// so the 64-bit buffer holds it; its multiplier 0x800000 >> (nv + 15) is
-// 1 << level for level <= 23.  Returns the two LUT entries.
-__device__ __forceinline__ void step_pair(uint64_t &buf, int &nv, uint32_t &off, uint32_t base,
-                                          uint32_t lut, uint32_t lenlut, unsigned lt,
-                                          uint32_t &e0, uint32_t &e1) {
+// Decode table: per warp, 512 16-bit entries len | sym << 12 built from the
+// row's 512-byte LUT (sym << 4 | len), the entry of window w at byte 2w of a
+// 1 KiB-aligned block.  Bit buffer: the lane's stream bits sit one bit up in a
+// 64-bit register pair (stream bit j at bit j + 1), so a window's table
+// address is one AND/OR of the register holding it ((x & 0x3FE) | table).
+// An entry's low five bits are its code length (bits 5-11 are zero), which is
+// all a wrapping funnel shift reads of its shift amount: the next window is
+// shf.r.wrap(lo, hi, entry), the sum of a round's entries shifts the buffer,
+// and the symbol bits above never matter.
+//
+// Level counter: nv = (26 - level) << 25 (the lane's valid bit count in the
+// top seven bits).  A lane refills before a symbol iff level < 9 there, i.e.
+// nv + (lengths of the round's earlier symbols) << 25 >= 18 << 25; an entry
+// times 2^25 is exactly its length << 25 (the symbol bits leave the register),
+// so every level update is one multiply-add on the FMA pipe.  The insert
+// multiplier 2^(level + 1) = 2^27 >> (nv >> 25) for a refilling lane.
+constexpr int kNvStart = 26 << 25;  // level 0
+
+// Three symbols per ballot round: after a refill a lane holds at least 32 bits,
+// so it cannot refill again within the next two symbols; each lane refills at
+// most once in three consecutive symbols.  Its refill symbol k (level < 9 before
+// symbol k) is known before the word arrives: the round's first two entries are
+// looked up in the current buffer, exact for every symbol before a lane's
+// refill symbol (>= 9 valid bits there).  Three cumulative ballots (refill at a
+// slot <= 0, <= 1, <= 2) order the refills as the format does (symbol i's
+// refilling lanes in lane order, then i+1's, then i+2's); a lane's word index
+// is popc(B_{k-1} | (B_k & lanes below it)), one shared load gives each
+// refilling lane its word, and the word goes in right above the lane's valid
+// bits before symbol i (at most bit 27 with the one-bit offset: level < 9 + two
+// codes of at most 9 bits), where the 64-bit buffer holds it.  Then the
+// symbols are decoded from the new buffer; the first two are looked up again
+// only by the lanes whose refill came at or before them (predicated loads: the
+// other lanes' entries from the current buffer are already exact), the third
+// by every lane.  Returns the three table entries.
+__device__ __forceinline__ void round3(uint64_t &buf, int &nv, uint32_t &off, uint32_t ring,
+                                       uint32_t tab, uint32_t msk, unsigned lt, uint32_t &e0,
+                                       uint32_t &e1, uint32_t &e2) {
+  const uint32_t k25 = 1u << 25;
   asm volatile(
       "{\n\t"
-      ".reg .pred p0, ev;\n\t"
-      ".reg .b32 x, ia, l0, t, b0, b1, n0, n1, mb, c, a, w, m, len;\n\t"
-      "setp.ge.s32 p0, %1, 0;\n\t"
-      "cvt.u32.u64 x, %0;\n\t"
-      "and.b32 ia, x, 511;\n\t"
-      "or.b32 ia, ia, %8;\n\t"
-      "ld.shared.u8 l0, [ia];\n\t"
-      "add.s32 t, %1, l0;\n\t"
-      "setp.ge.s32 ev, t, 0;\n\t"
+      ".reg .pred p0, q, ev;\n\t"
+      ".reg .b32 lo, hi, x, a, t1, t2, b0, b1, b2, mb, bs, c, n2, w, m, s, z;\n\t"
+      "mov.b32 z, 0;\n\t"
+      "mov.b64 {lo, hi}, %0;\n\t"
+      "and.b32 a, lo, %10;\n\t"
+      "or.b32 a, a, %7;\n\t"
+      "ld.shared.u16 %3, [a];\n\t"
+      "shf.r.wrap.b32 x, lo, hi, %3;\n\t"
+      "and.b32 a, x, %10;\n\t"
+      "or.b32 a, a, %7;\n\t"
+      "ld.shared.u16 %4, [a];\n\t"
+      "mad.lo.u32 t1, %3, %9, %1;\n\t"
+      "mad.lo.u32 t2, %4, %9, t1;\n\t"
+      "setp.ge.s32 p0, %1, 603979776;\n\t"
+      "setp.ge.s32 q, t1, 603979776;\n\t"
+      "setp.ge.s32 ev, t2, 603979776;\n\t"
       "vote.sync.ballot.b32 b0, p0, 0xffffffff;\n\t"
-      "vote.sync.ballot.b32 b1, ev, 0xffffffff;\n\t"
-      "selp.b32 n0, 0, b0, p0;\n\t"
-      "selp.b32 mb, b0, b1, p0;\n\t"
-      "lop3.b32 mb, mb, n0, %5, 0xE4;\n\t"
+      "vote.sync.ballot.b32 b1, q, 0xffffffff;\n\t"
+      "vote.sync.ballot.b32 b2, ev, 0xffffffff;\n\t"
+      "selp.b32 bs, b1, b2, q;\n\t"
+      "selp.b32 bs, b0, bs, p0;\n\t"
+      "selp.b32 mb, b0, b1, q;\n\t"
+      "selp.b32 mb, 0, mb, p0;\n\t"
+      "lop3.b32 mb, bs, mb, %8, 0xE4;\n\t"
       "popc.b32 c, mb;\n\t"
       "mad.lo.u32 a, c, 4, %2;\n\t"
       "and.b32 a, a, " XP_RING_MASK ";\n\t"
       "or.b32 a, a, %6;\n\t"
       "ld.shared.u32 w, [a];\n\t"
-      "popc.b32 n1, b1;\n\t"
-      "mad.lo.u32 %2, n1, 4, %2;\n\t"
-      "add.s32 t, %1, 15;\n\t"
-      "shr.b32 m, 8388608, t;\n\t"
+      "popc.b32 n2, b2;\n\t"
+      "mad.lo.u32 %2, n2, 4, %2;\n\t"
+      "shr.u32 s, %1, 25;\n\t"
+      "shr.b32 m, 134217728, s;\n\t"
       "@ev mad.wide.u32 %0, w, m, %0;\n\t"
-      "@ev add.s32 %1, %1, -32;\n\t"
-      "cvt.u32.u64 x, %0;\n\t"
-      "and.b32 x, x, 511;\n\t"
-      "or.b32 x, x, %7;\n\t"
-      "ld.shared.u8 %3, [x];\n\t"
-      "and.b32 len, %3, 15;\n\t"
-      "shr.b64 %0, %0, len;\n\t"
-      "add.s32 %1, %1, len;\n\t"
-      "cvt.u32.u64 x, %0;\n\t"
-      "and.b32 x, x, 511;\n\t"
-      "or.b32 x, x, %7;\n\t"
-      "ld.shared.u8 %4, [x];\n\t"
-      "and.b32 len, %4, 15;\n\t"
-      "shr.b64 %0, %0, len;\n\t"
-      "add.s32 %1, %1, len;\n\t"
+      "@ev add.s32 %1, %1, -1073741824;\n\t"
+      "mov.b64 {lo, hi}, %0;\n\t"
+      "and.b32 a, lo, %10;\n\t"
+      "or.b32 a, a, %7;\n\t"
+      "@p0 ld.shared.u16 %3, [a];\n\t"
+      "shf.r.wrap.b32 x, lo, hi, %3;\n\t"
+      "and.b32 a, x, %10;\n\t"
+      "or.b32 a, a, %7;\n\t"
+      "@q ld.shared.u16 %4, [a];\n\t"
+      "shf.r.wrap.b32 x, x, z, %4;\n\t"
+      "and.b32 a, x, %10;\n\t"
+      "or.b32 a, a, %7;\n\t"
+      "ld.shared.u16 %5, [a];\n\t"
+      "add.s32 s, %3, %4;\n\t"
+      "add.s32 s, s, %5;\n\t"
+      "shf.r.wrap.b32 x, lo, hi, s;\n\t"
+      "shf.r.wrap.b32 hi, hi, z, s;\n\t"
+      "mov.b64 %0, {x, hi};\n\t"
+      "mad.lo.u32 %1, s, %9, %1;\n\t"
       "}"
-      : "+l"(buf), "+r"(nv), "+r"(off), "=&r"(e0), "=&r"(e1)
-      : "r"(lt), "r"(base), "r"(lut), "r"(lenlut));
+      : "+l"(buf), "+r"(nv), "+r"(off), "=&r"(e0), "=&r"(e1), "=&r"(e2)
+      : "r"(ring), "r"(tab), "r"(lt), "r"(k25), "r"(msk));
 }
 
-
-// Three symbols per ballot round: after a refill a lane holds at least 32 bits,
-// so it cannot refill again within the next two symbols; each lane refills at
-// most once in three consecutive symbols.  Its refill symbol k (level < 9 before
-// symbol k, the earlier symbols' lengths from two chained length-only lookups
-// of the current buffer) is known before any of the three is decoded; three
-// cumulative ballots (refills at a slot <= 0, <= 1, <= 2; as in step_pair each
-// follows from one comparison, nv + len_i + ... >= 0) order the refills as the
-// format does (symbol i's refilling lanes in lane order, then i+1's, then
-// i+2's), each lane's word index from one popc as in step_pair, and the word
-// goes in right above the
-// lane's valid bits before symbol i, at most 26 bits up (level < 9 + two codes
-// of at most 9 bits), where the 64-bit buffer holds it; its multiplier
-// 0x4000000 >> (nv + 18) is 1 << level for level <= 26.
-__device__ __forceinline__ void step_triple(uint64_t &buf, int &nv, uint32_t &off, uint32_t base,
-                                            uint32_t lut, uint32_t lenlut, unsigned lt,
-                                            uint32_t &e0, uint32_t &e1, uint32_t &e2) {
+// Two symbols per ballot round, as round3 with one look-ahead entry: a lane
+// refills at symbol i (level < 9) or at i+1 (level - len_i < 9), and the
+// word goes in at most at bit 18.  Returns the two table entries.
+__device__ __forceinline__ void round2(uint64_t &buf, int &nv, uint32_t &off, uint32_t ring,
+                                       uint32_t tab, uint32_t msk, unsigned lt, uint32_t &e0,
+                                       uint32_t &e1) {
+  const uint32_t k25 = 1u << 25;
   asm volatile(
       "{\n\t"
-      ".reg .pred p0, q, ev;\n\t"
-      ".reg .b32 x, lo, hi, l0, l1, t, b0, b1, b2, n1, mb, c, bs, a, w, m, len;\n\t"
-      "setp.ge.s32 p0, %1, 0;\n\t"
+      ".reg .pred p0, ev;\n\t"
+      ".reg .b32 lo, hi, x, a, t1, b0, b1, mb, bs, c, n1, w, m, s, z;\n\t"
+      "mov.b32 z, 0;\n\t"
       "mov.b64 {lo, hi}, %0;\n\t"
-      "and.b32 x, lo, 511;\n\t"
-      "or.b32 x, x, %9;\n\t"
-      "ld.shared.u8 l0, [x];\n\t"
-      "shf.r.clamp.b32 x, lo, hi, l0;\n\t"
-      "and.b32 x, x, 511;\n\t"
-      "or.b32 x, x, %9;\n\t"
-      "ld.shared.u8 l1, [x];\n\t"
-      "add.s32 t, %1, l0;\n\t"
-      "setp.ge.s32 q, t, 0;\n\t"
-      "add.s32 t, t, l1;\n\t"
-      "setp.ge.s32 ev, t, 0;\n\t"
+      "and.b32 a, lo, %9;\n\t"
+      "or.b32 a, a, %6;\n\t"
+      "ld.shared.u16 %3, [a];\n\t"
+      "mad.lo.u32 t1, %3, %8, %1;\n\t"
+      "setp.ge.s32 p0, %1, 603979776;\n\t"
+      "setp.ge.s32 ev, t1, 603979776;\n\t"
       "vote.sync.ballot.b32 b0, p0, 0xffffffff;\n\t"
-      "vote.sync.ballot.b32 b1, q, 0xffffffff;\n\t"
-      "vote.sync.ballot.b32 b2, ev, 0xffffffff;\n\t"
-      "selp.b32 mb, b0, b1, q;\n\t"
-      "selp.b32 mb, 0, mb, p0;\n\t"
-      "selp.b32 bs, b1, b2, q;\n\t"
-      "selp.b32 bs, b0, bs, p0;\n\t"
-      "lop3.b32 mb, bs, mb, %6, 0xE4;\n\t"
+      "vote.sync.ballot.b32 b1, ev, 0xffffffff;\n\t"
+      "selp.b32 mb, 0, b0, p0;\n\t"
+      "selp.b32 bs, b0, b1, p0;\n\t"
+      "lop3.b32 mb, bs, mb, %7, 0xE4;\n\t"
       "popc.b32 c, mb;\n\t"
       "mad.lo.u32 a, c, 4, %2;\n\t"
       "and.b32 a, a, " XP_RING_MASK ";\n\t"
-      "or.b32 a, a, %7;\n\t"
+      "or.b32 a, a, %5;\n\t"
       "ld.shared.u32 w, [a];\n\t"
-      "popc.b32 n1, b2;\n\t"
+      "popc.b32 n1, b1;\n\t"
       "mad.lo.u32 %2, n1, 4, %2;\n\t"
-      "add.s32 t, %1, 18;\n\t"
-      "shr.b32 m, 67108864, t;\n\t"
+      "shr.u32 s, %1, 25;\n\t"
+      "shr.b32 m, 134217728, s;\n\t"
       "@ev mad.wide.u32 %0, w, m, %0;\n\t"
-      "@ev add.s32 %1, %1, -32;\n\t"
-      "cvt.u32.u64 x, %0;\n\t"
-      "and.b32 x, x, 511;\n\t"
-      "or.b32 x, x, %8;\n\t"
-      "ld.shared.u8 %3, [x];\n\t"
-      "and.b32 len, %3, 15;\n\t"
-      "shr.b64 %0, %0, len;\n\t"
-      "add.s32 %1, %1, len;\n\t"
-      "cvt.u32.u64 x, %0;\n\t"
-      "and.b32 x, x, 511;\n\t"
-      "or.b32 x, x, %8;\n\t"
-      "ld.shared.u8 %4, [x];\n\t"
-      "and.b32 len, %4, 15;\n\t"
-      "shr.b64 %0, %0, len;\n\t"
-      "add.s32 %1, %1, len;\n\t"
-      "cvt.u32.u64 x, %0;\n\t"
-      "and.b32 x, x, 511;\n\t"
-      "or.b32 x, x, %8;\n\t"
-      "ld.shared.u8 %5, [x];\n\t"
-      "and.b32 len, %5, 15;\n\t"
-      "shr.b64 %0, %0, len;\n\t"
-      "add.s32 %1, %1, len;\n\t"
+      "@ev add.s32 %1, %1, -1073741824;\n\t"
+      "mov.b64 {lo, hi}, %0;\n\t"
+      "and.b32 a, lo, %9;\n\t"
+      "or.b32 a, a, %6;\n\t"
+      "@p0 ld.shared.u16 %3, [a];\n\t"
+      "shf.r.wrap.b32 x, lo, hi, %3;\n\t"
+      "and.b32 a, x, %9;\n\t"
+      "or.b32 a, a, %6;\n\t"
+      "ld.shared.u16 %4, [a];\n\t"
+      "add.s32 s, %3, %4;\n\t"
+      "shf.r.wrap.b32 x, lo, hi, s;\n\t"
+      "shf.r.wrap.b32 hi, hi, z, s;\n\t"
+      "mov.b64 %0, {x, hi};\n\t"
+      "mad.lo.u32 %1, s, %8, %1;\n\t"
       "}"
-      : "+l"(buf), "+r"(nv), "+r"(off), "=&r"(e0), "=&r"(e1), "=&r"(e2)
-      : "r"(lt), "r"(base), "r"(lut), "r"(lenlut));
+      : "+l"(buf), "+r"(nv), "+r"(off), "=&r"(e0), "=&r"(e1)
+      : "r"(ring), "r"(tab), "r"(lt), "r"(k25), "r"(msk));
 }
 
 __device__ __forceinline__ void cp_async16_s(uint32_t saddr, const void *gmem) {
@@ -322,10 +329,16 @@ __device__ __forceinline__ void ring_fill(uint32_t base, const uint8_t *src, uin
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
+// V8: the output goes out as one 32-byte store per lane per 32 symbols (rows
+// 32-byte aligned and chunk a multiple of 32), else one 16-byte store per 16
+// symbols.  Each lane's stores land 512 bytes (its chunk) from its neighbours',
+// so a warp's store touches 32 lines whatever its width; twice the bytes per
+// store halves the store traffic through the L1 data pipe, which this kernel
+// shares with its table lookups.
+template <bool V8>
 __global__ void __launch_bounds__(kWarps * 32, 10) decode_ring_kernel(const __grid_constant__ DecodeArgs a) {
   extern __shared__ __align__(16) uint8_t s_dyn[];  // kWarps rings of 2 KiB, 2 KiB-aligned
-  __shared__ __align__(512) uint8_t s_lut[kWarps][kLutBytes];
-  __shared__ __align__(512) uint8_t s_len[kWarps][kLutBytes];  // lengths only
+  __shared__ __align__(1024) uint16_t s_tab[kWarps][kLutBytes];  // len | sym << 12
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t j = blockIdx.y;
   const int64_t gg = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
@@ -359,11 +372,32 @@ __global__ void __launch_bounds__(kWarps * 32, 10) decode_ring_kernel(const __gr
   const int64_t wmax = rec_w - huff_w;
   w_end = w_end < 0 ? 0 : (w_end > wmax ? wmax : w_end);
   w_begin = w_begin < 0 ? 0 : (w_begin > w_end ? w_end : w_begin);
-  uint8_t *L = s_lut[warp];
-  reinterpret_cast<uint4 *>(L)[lane] = lut_v;
-  reinterpret_cast<uint4 *>(s_len[warp])[lane] =
-      make_uint4(lut_v.x & 0x0F0F0F0Fu, lut_v.y & 0x0F0F0F0Fu, lut_v.z & 0x0F0F0F0Fu,
-                 lut_v.w & 0x0F0F0F0Fu);
+  // The decode table: LUT byte sym << 4 | len -> 16-bit len | sym << 12, each
+  // lane converting its 16 bytes (two per 32-bit word).
+  uint16_t *T = s_tab[warp];
+  {
+    const uint32_t v[4] = {lut_v.x, lut_v.y, lut_v.z, lut_v.w};
+    uint32_t t[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t b = __byte_perm(v[i / 2], 0, (i & 1) ? 0x4342 : 0x4140);  // bytes -> halves
+      t[i] = (b & 0x000F000Fu) | ((b & 0x00F000F0u) << 8);
+    }
+    reinterpret_cast<uint4 *>(T)[2 * lane] = make_uint4(t[0], t[1], t[2], t[3]);
+    reinterpret_cast<uint4 *>(T)[2 * lane + 1] = make_uint4(t[4], t[5], t[6], t[7]);
+  }
+  // Windows are looked up with as many bits as the row's longest code: the
+  // LUT repeats above that length, so entries [0, 2^maxlen) hold every code,
+  // and fewer distinct table words mean fewer shared-memory bank conflicts.
+  uint32_t msk;
+  {
+    const uint32_t m4 = __vmaxu4(__vmaxu4(lut_v.x & 0x0F0F0F0Fu, lut_v.y & 0x0F0F0F0Fu),
+                                 __vmaxu4(lut_v.z & 0x0F0F0F0Fu, lut_v.w & 0x0F0F0F0Fu));
+    uint32_t mx = max(max(m4 & 255, (m4 >> 8) & 255), max((m4 >> 16) & 255, m4 >> 24));
+    mx = __reduce_max_sync(kFull, mx);
+    mx = mx < 1 ? 1 : (mx > kLimit ? kLimit : mx);
+    msk = ((1u << mx) - 1) << 1;  // table byte offsets 2w of the used windows w
+  }
   dst_row = dst_row > 0 ? dst_row : 0;
   const uint32_t *nib = reinterpret_cast<const uint32_t *>(rec + head) + g * (chunk / 8) * 32;
   uint8_t *out_row = n.dst + dst_row * n.N + (g * 32 + lane) * chunk;
@@ -372,7 +406,7 @@ __global__ void __launch_bounds__(kWarps * 32, 10) decode_ring_kernel(const __gr
   if ((chunk / 8) % 2) {
     __syncwarp();
     decode_group_window(reinterpret_cast<const uint32_t *>(rec) + huff_w, w_begin, w_end, nib,
-                        out_row, chunk, L, lane);
+                        out_row, chunk, T, lane);
     return;
   }
   // The stream: bytes [0, total) from record word a0, in 16-byte units (the
@@ -389,19 +423,33 @@ __global__ void __launch_bounds__(kWarps * 32, 10) decode_ring_kernel(const __gr
 
   const unsigned lt = lanemask_lt();
   uint64_t buf = 0;
-  int nv = 8;  // 8 - level: level < 9 (a refill) iff nv >= 0
+  int nv = kNvStart;
   uint32_t off = static_cast<uint32_t>(4 * (a_begin - a0));
-  const uint32_t sl = static_cast<uint32_t>(__cvta_generic_to_shared(L));
-  const uint32_t sn = static_cast<uint32_t>(__cvta_generic_to_shared(s_len[warp]));
-  // Eight symbols in rounds of 3 + 3 + 2: their LUT entries summed at byte
-  // offsets, symbols 0-3 into lo and 4-7 into hi.
-  auto octet = [&](uint32_t &lo, uint32_t &hi) {
+  const uint32_t tab = static_cast<uint32_t>(__cvta_generic_to_shared(T));
+  // Exponent fields of 4 symbols from their table entries len | sym << 12:
+  // sym << (8k + 3) for symbol k, by e >> 9, e >> 1, e << 7, e << 15 as
+  // multiplies.  The length bits those leave behind (len >> 1 at bits 0-2,
+  // len << 7 at bits 7-10, len << 15 at bits 15-18) share no bit with the
+  // exponent fields (bits 3-6 of each byte) or with one another, so the sum
+  // carries nowhere and the caller keeps bits 3-6 of each byte.
+  auto pack4 = [&](uint32_t e0, uint32_t e1, uint32_t e2, uint32_t e3) {
+    return mad_u32(e3, 1u << 15, mad_u32(e2, 1u << 7, madhi_u32(e1, 1u << 31, mulhi_u32(e0, 1u << 23))));
+  };
+  // Eight symbols in rounds of 3 + 3 + 2 -> two output words: nibble word nw
+  // holds the 8 sign/mantissa nibbles (symbol k at bits 4k..4k+3).  Nibbles
+  // 0, 2, 4, 6 and 1, 3, 5, 7 go to the low halves of the bytes of two words,
+  // times 17 copies each to its byte's high half, a byte permute interleaves
+  // them in symbol order, and one select keeps the sign (bit 7) and mantissa
+  // (bits 0-2) from there and the exponent (bits 3-6) from the entries.
+  auto octet = [&](uint32_t nw, uint32_t &lo, uint32_t &hi) {
     uint32_t e[8];
-    step_triple(buf, nv, off, base, sl, sn, lt, e[0], e[1], e[2]);
-    step_triple(buf, nv, off, base, sl, sn, lt, e[3], e[4], e[5]);
-    step_pair(buf, nv, off, base, sl, sn, lt, e[6], e[7]);
-    lo = mad_u32(e[3], 1u << 24, mad_u32(e[2], 1u << 16, mad_u32(e[1], 1u << 8, e[0])));
-    hi = mad_u32(e[7], 1u << 24, mad_u32(e[6], 1u << 16, mad_u32(e[5], 1u << 8, e[4])));
+    round3(buf, nv, off, base, tab, msk, lt, e[0], e[1], e[2]);
+    round3(buf, nv, off, base, tab, msk, lt, e[3], e[4], e[5]);
+    round2(buf, nv, off, base, tab, msk, lt, e[6], e[7]);
+    const uint32_t ev = mul_u32(nw & 0x0F0F0F0Fu, 17u);
+    const uint32_t od = mul_u32(mulhi_u32(nw, 1u << 28) & 0x0F0F0F0Fu, 17u);
+    lo = bitsel(pack4(e[0], e[1], e[2], e[3]), __byte_perm(ev, od, 0x5140), 0x78787878u);
+    hi = bitsel(pack4(e[4], e[5], e[6], e[7]), __byte_perm(ev, od, 0x7362), 0x78787878u);
   };
   const int64_t steps = chunk / 8;
   const int64_t last = steps - 1;
@@ -411,10 +459,9 @@ __global__ void __launch_bounds__(kWarps * 32, 10) decode_ring_kernel(const __gr
   uint32_t q1 = __ldg(nib + 32 + lane);
   uint32_t q2 = __ldg(nib + (2 < last ? 2 : last) * 32 + lane);
   uint32_t q3 = __ldg(nib + (3 < last ? 3 : last) * 32 + lane);
-  uint4 *out = reinterpret_cast<uint4 *>(out_row);
-#pragma unroll 2
-  for (int64_t m = 0; m < steps; m += 2) {
-    // Ring upkeep, warp-uniform (off and filled are the same in every lane).
+  // Ring upkeep at the top of every 16 symbols, warp-uniform (off and filled
+  // are the same in every lane).
+  auto upkeep = [&]() {
     if (filled < total && off + kHalf >= filled) {
       const uint32_t hi = filled + kHalf < total ? filled + kHalf : total;
       ring_fill(base, src, filled, hi, lane);
@@ -426,22 +473,38 @@ __global__ void __launch_bounds__(kWarps * 32, 10) decode_ring_kernel(const __gr
       __syncwarp();
       pending = false;
     }
-    uint32_t lohi[4];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const uint32_t nw = h ? q1 : q0;
-      uint32_t acc_lo, acc_hi;
-      octet(acc_lo, acc_hi);
-      lohi[2 * h] = merge4(acc_lo, nw & 0xFFFFu);
-      lohi[2 * h + 1] = merge4(acc_hi, nw >> 16);
-    }
-    out[m / 2] = make_uint4(lohi[0], lohi[1], lohi[2], lohi[3]);
+  };
+  // Sixteen symbols: two octets from the nibble words q0, q1; then the nibble
+  // words move up and the next two are loaded (two iterations ahead).
+  auto sixteen = [&](int64_t m, uint32_t *w) {
+    upkeep();
+    octet(q0, w[0], w[1]);
+    octet(q1, w[2], w[3]);
     q0 = q2;
     q1 = q3;
     if (lane < 2 && m + 16 + lane <= last)
       asm volatile("prefetch.global.L2 [%0];" ::"l"(nib + (m + 16 + lane) * 32));
     q2 = __ldg(nib + (m + 4 < last ? m + 4 : last) * 32 + lane);
     q3 = __ldg(nib + (m + 5 < last ? m + 5 : last) * 32 + lane);
+  };
+  if (V8) {
+    for (int64_t m = 0; m < steps; m += 4) {
+      uint32_t w[8];
+      sixteen(m, w);
+      sixteen(m + 2, w + 4);
+      asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(out_row + m * 8),
+                   "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]),
+                   "r"(w[7])
+                   : "memory");
+    }
+  } else {
+    uint4 *out = reinterpret_cast<uint4 *>(out_row);
+#pragma unroll 2
+    for (int64_t m = 0; m < steps; m += 2) {
+      uint32_t w[4];
+      sixteen(m, w);
+      out[m / 2] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
   }
   // Leave no copy in flight into shared memory at exit.
   asm volatile("cp.async.wait_group 0;" ::: "memory");
@@ -484,6 +547,12 @@ extern "C" int xp_decode_rows(const int64_t *todo, int64_t K, const int64_t *dst
   }
   const int64_t groups = a.n[0].G + a.n[1].G;
   dim3 grid(static_cast<unsigned>((groups + kWarps - 1) / kWarps), static_cast<unsigned>(K));
-  decode_ring_kernel<<<grid, kWarps * 32, kRingSmem, as_stream(stream)>>>(a);
+  // 32-byte stores when every lane chunk starts on a 32-byte boundary and
+  // holds a whole number of 32-symbol blocks.
+  const bool v8 = chunk % 32 == 0 && aligned(dst0, 32) && aligned(dst1, 32);
+  if (v8)
+    decode_ring_kernel<true><<<grid, kWarps * 32, kRingSmem, as_stream(stream)>>>(a);
+  else
+    decode_ring_kernel<false><<<grid, kWarps * 32, kRingSmem, as_stream(stream)>>>(a);
   return launch_status();
 }
