@@ -264,8 +264,9 @@ int xp_decode_step_noalloc(const void *topk_ids, int ids_bytes, int64_t K, int64
  * todo[j] = e >= 0 with cache_row[e] < 0 (and e not in skip[0:K] if skip is
  * not NULL): expand record stg_n[j] (P_n bytes per row) into dst_n[dst_row[e]]
  * (N_n bytes per row) with the LUT lut[e][n] (uint8[E][2][512]), n = 0, 1.
- * chunk: values per lane (512 in production; multiple of 8; N_n a multiple of
- * 32*chunk).  Records are in the reference's format (codec.py:22-26). */
+ * chunk: values per lane (512 in production; multiple of 8, at most 2^30; N_n
+ * a multiple of 32*chunk).  Records are in the reference's format
+ * (codec.py:22-26). */
 int xp_decode_rows(const int64_t *todo, int64_t K, const int64_t *dst_row,
                    const int64_t *cache_row, const uint8_t *lut,
                    const void *stg0, int64_t P0, void *dst0, int64_t N0,

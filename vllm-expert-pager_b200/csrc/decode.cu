@@ -35,8 +35,8 @@
 //    exponent fields are packed by multiplies too, and the sign/mantissa
 //    nibbles spread by multiplies and one byte permute.  The integer ALU pipe
 //    (one warp instruction per two cycles per scheduler) takes the rest.
-//  * Each lane stores 16 bytes per 16 symbols; nibble words are loaded two
-//    iterations ahead and prefetched into L2 eight iterations ahead.
+//  * Each lane stores 32 bytes per 32 symbols (16 per 16 where rows are not
+//    32-byte aligned); nibble words are loaded 32 symbols ahead.
 #include "common.cuh"
 
 namespace xp {
@@ -193,7 +193,8 @@ constexpr int kNvStart = 26 << 25;  // level 0
 // slot <= 0, <= 1, <= 2) order the refills as the format does (symbol i's
 // refilling lanes in lane order, then i+1's, then i+2's); a lane's word index
 // is popc(B_{k-1} | (B_k & lanes below it)), one shared load gives each
-// refilling lane its word, and the word goes in right above the lane's valid
+// refilling lane its word (the others keep a zero word, so the insert itself
+// needs no predicate), and the word goes in right above the lane's valid
 // bits before symbol i (at most bit 27 with the one-bit offset: level < 9 + two
 // codes of at most 9 bits), where the 64-bit buffer holds it.  Then the
 // symbols are decoded from the new buffer; the first two are looked up again
@@ -209,6 +210,7 @@ __device__ __forceinline__ void round3(uint64_t &buf, int &nv, uint32_t &off, ui
       ".reg .pred p0, q, ev;\n\t"
       ".reg .b32 lo, hi, x, a, t1, t2, b0, b1, b2, mb, bs, c, n2, w, m, s, z;\n\t"
       "mov.b32 z, 0;\n\t"
+      "mov.b32 w, 0;\n\t"
       "mov.b64 {lo, hi}, %0;\n\t"
       "and.b32 a, lo, %10;\n\t"
       "or.b32 a, a, %7;\n\t"
@@ -234,12 +236,12 @@ __device__ __forceinline__ void round3(uint64_t &buf, int &nv, uint32_t &off, ui
       "mad.lo.u32 a, c, 4, %2;\n\t"
       "and.b32 a, a, " XP_RING_MASK ";\n\t"
       "or.b32 a, a, %6;\n\t"
-      "ld.shared.u32 w, [a];\n\t"
+      "@ev ld.shared.u32 w, [a];\n\t"
       "popc.b32 n2, b2;\n\t"
       "mad.lo.u32 %2, n2, 4, %2;\n\t"
       "shr.u32 s, %1, 25;\n\t"
       "shr.b32 m, 134217728, s;\n\t"
-      "@ev mad.wide.u32 %0, w, m, %0;\n\t"
+      "mad.wide.u32 %0, w, m, %0;\n\t"
       "@ev add.s32 %1, %1, -1073741824;\n\t"
       "mov.b64 {lo, hi}, %0;\n\t"
       "and.b32 a, lo, %10;\n\t"
@@ -276,6 +278,7 @@ __device__ __forceinline__ void round2(uint64_t &buf, int &nv, uint32_t &off, ui
       ".reg .pred p0, ev;\n\t"
       ".reg .b32 lo, hi, x, a, t1, b0, b1, mb, bs, c, n1, w, m, s, z;\n\t"
       "mov.b32 z, 0;\n\t"
+      "mov.b32 w, 0;\n\t"
       "mov.b64 {lo, hi}, %0;\n\t"
       "and.b32 a, lo, %9;\n\t"
       "or.b32 a, a, %6;\n\t"
@@ -292,12 +295,12 @@ __device__ __forceinline__ void round2(uint64_t &buf, int &nv, uint32_t &off, ui
       "mad.lo.u32 a, c, 4, %2;\n\t"
       "and.b32 a, a, " XP_RING_MASK ";\n\t"
       "or.b32 a, a, %5;\n\t"
-      "ld.shared.u32 w, [a];\n\t"
+      "@ev ld.shared.u32 w, [a];\n\t"
       "popc.b32 n1, b1;\n\t"
       "mad.lo.u32 %2, n1, 4, %2;\n\t"
       "shr.u32 s, %1, 25;\n\t"
       "shr.b32 m, 134217728, s;\n\t"
-      "@ev mad.wide.u32 %0, w, m, %0;\n\t"
+      "mad.wide.u32 %0, w, m, %0;\n\t"
       "@ev add.s32 %1, %1, -1073741824;\n\t"
       "mov.b64 {lo, hi}, %0;\n\t"
       "and.b32 a, lo, %9;\n\t"
@@ -451,14 +454,16 @@ __global__ void __launch_bounds__(kWarps * 32, 10) decode_ring_kernel(const __gr
     lo = bitsel(pack4(e[0], e[1], e[2], e[3]), __byte_perm(ev, od, 0x5140), 0x78787878u);
     hi = bitsel(pack4(e[4], e[5], e[6], e[7]), __byte_perm(ev, od, 0x7362), 0x78787878u);
   };
-  const int64_t steps = chunk / 8;
-  const int64_t last = steps - 1;
-  for (int64_t i = lane; i < 16 && i <= last; i += 32)
-    asm volatile("prefetch.global.L2 [%0];" ::"l"(nib + i * 32));
-  uint32_t q0 = __ldg(nib + lane);
-  uint32_t q1 = __ldg(nib + 32 + lane);
-  uint32_t q2 = __ldg(nib + (2 < last ? 2 : last) * 32 + lane);
-  uint32_t q3 = __ldg(nib + (3 < last ? 3 : last) * 32 + lane);
+  const int steps = static_cast<int>(chunk / 8);
+  // Nibble words of 8-value block k: np[32 k]; q0..q3 hold blocks m..m+3.
+  const uint32_t *np = nib + lane;
+  uint32_t q0 = __ldg(np);
+  uint32_t q1 = __ldg(np + 32);
+  uint32_t q2 = 0, q3 = 0;
+  if (steps > 2) {
+    q2 = __ldg(np + 64);
+    q3 = __ldg(np + 96);
+  }
   // Ring upkeep at the top of every 16 symbols, warp-uniform (off and filled
   // are the same in every lane).
   auto upkeep = [&]() {
@@ -475,24 +480,26 @@ __global__ void __launch_bounds__(kWarps * 32, 10) decode_ring_kernel(const __gr
     }
   };
   // Sixteen symbols: two octets from the nibble words q0, q1; then the nibble
-  // words move up and the next two are loaded (two iterations ahead).
-  auto sixteen = [&](int64_t m, uint32_t *w) {
+  // words move up and the next two are loaded (two iterations ahead; none past
+  // the group's last block, steps being even).
+  auto sixteen = [&](int m, uint32_t *w) {
     upkeep();
     octet(q0, w[0], w[1]);
     octet(q1, w[2], w[3]);
     q0 = q2;
     q1 = q3;
-    if (lane < 2 && m + 16 + lane <= last)
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(nib + (m + 16 + lane) * 32));
-    q2 = __ldg(nib + (m + 4 < last ? m + 4 : last) * 32 + lane);
-    q3 = __ldg(nib + (m + 5 < last ? m + 5 : last) * 32 + lane);
+    np += 64;
+    if (m + 4 < steps) {
+      q2 = __ldg(np + 64);
+      q3 = __ldg(np + 96);
+    }
   };
   if (V8) {
-    for (int64_t m = 0; m < steps; m += 4) {
+    for (int m = 0; m < steps; m += 4) {
       uint32_t w[8];
       sixteen(m, w);
       sixteen(m + 2, w + 4);
-      asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(out_row + m * 8),
+      asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(out_row + 8 * m),
                    "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]),
                    "r"(w[7])
                    : "memory");
@@ -500,7 +507,7 @@ __global__ void __launch_bounds__(kWarps * 32, 10) decode_ring_kernel(const __gr
   } else {
     uint4 *out = reinterpret_cast<uint4 *>(out_row);
 #pragma unroll 2
-    for (int64_t m = 0; m < steps; m += 2) {
+    for (int m = 0; m < steps; m += 2) {
       uint32_t w[4];
       sixteen(m, w);
       out[m / 2] = make_uint4(w[0], w[1], w[2], w[3]);
@@ -520,7 +527,7 @@ extern "C" int xp_decode_rows(const int64_t *todo, int64_t K, const int64_t *dst
                               int64_t P0, void *dst0, int64_t N0, const void *stg1, int64_t P1,
                               void *dst1, int64_t N1, const int64_t *skip, int64_t chunk,
                               void *stream) {
-  if (K < 0 || K > 65535 || chunk < 8 || chunk % 8) return XP_EINVAL;
+  if (K < 0 || K > 65535 || chunk < 8 || chunk % 8 || chunk > (int64_t(1) << 30)) return XP_EINVAL;
   if (K == 0) return XP_OK;
   if (!todo || !dst_row || !cache_row || !lut || !aligned(lut, 16)) return XP_EINVAL;
   DecodeArgs a{};
