@@ -73,6 +73,35 @@ def test_random_distributions_match_oracle(seed):
     assert np.array_equal(a, raw)
 
 
+@pytest.mark.parametrize("chunk,offset", [(512, 16), (48, 0), (80, 16), (512, 0)])
+def test_store_widths_decode_alike(chunk, offset):
+    """The kernel stores 32 bytes per lane per 32 symbols when every lane chunk starts on a
+    32-byte boundary and holds whole 32-value blocks, else 16 bytes per 16 symbols: rows
+    that start 16 bytes into an allocation and chunks of 48 or 80 values take the 16-byte
+    stores, and both store paths leave the bytes around the rows untouched."""
+    from vllm_expert_pager import codec
+
+    rng = np.random.default_rng(chunk + offset)
+    n = 32 * chunk * 3
+    p = rng.dirichlet(np.full(16, 0.5))
+    raws = [rows(300 + chunk + k, n, p.tolist()).numpy() for k in range(2)]
+    encs = [oc.encode(r, oc.pitch_of(n, 1.5, 4096) + 4096, chunk) for r in raws]
+    stg = [torch.from_numpy(e[0].copy()).to(DEV).view(1, -1) for e in encs]
+    luts = torch.from_numpy(np.stack([encs[0][1], encs[1][1]])[None]).to(DEV)
+    backing = [torch.full((n + 64,), 0xA5, dtype=torch.uint8, device=DEV) for _ in range(2)]
+    dst = [b[offset: offset + n].view(1, n) for b in backing]
+    assert all(d.data_ptr() % 16 == 0 for d in dst)
+    todo = torch.zeros((1,), dtype=torch.int64, device=DEV)
+    dst_row = torch.zeros((1,), dtype=torch.int64, device=DEV)
+    cache_row = torch.full((1,), -1, dtype=torch.int64, device=DEV)
+    codec.decode_rows(todo, dst_row, cache_row, stg, dst, luts, chunk=chunk)
+    torch.cuda.synchronize()
+    for k in range(2):
+        b = backing[k].cpu().numpy()
+        assert np.array_equal(b[offset: offset + n], raws[k]), k
+        assert np.all(b[:offset] == 0xA5) and np.all(b[offset + n:] == 0xA5), k
+
+
 def _canonical(lut: np.ndarray) -> bool:
     """The decoder's fast-path rule: each window's code length is 1 + the number of
     thresholds lim[L] (windows with codes of at most L bits) that the window, read
