@@ -169,8 +169,9 @@ constexpr size_t kRingSmem = kWarps * kRing + kRing;
 // Decode table: per warp, 512 16-bit entries len | sym << 12 built from the
 // row's 512-byte LUT (sym << 4 | len), the entry of window w at byte 2w of a
 // 1 KiB-aligned block.  Bit buffer: the lane's stream bits sit one bit up in a
-// 64-bit register pair (stream bit j at bit j + 1), so a window's table
-// address is one AND/OR of the register holding it ((x & 0x3FE) | table).
+// 64-bit register pair lo, hi (stream bit j at bit j + 1), so a window's table
+// address is one AND/OR of the register holding it ((x & mask) | table, the
+// mask keeping as many window bits as the row's longest code).
 // An entry's low five bits are its code length (bits 5-11 are zero), which is
 // all a wrapping funnel shift reads of its shift amount: the next window is
 // shf.r.wrap(lo, hi, entry), the sum of a round's entries shifts the buffer,
@@ -180,8 +181,10 @@ constexpr size_t kRingSmem = kWarps * kRing + kRing;
 // top seven bits).  A lane refills before a symbol iff level < 9 there, i.e.
 // nv + (lengths of the round's earlier symbols) << 25 >= 18 << 25; an entry
 // times 2^25 is exactly its length << 25 (the symbol bits leave the register),
-// so every level update is one multiply-add on the FMA pipe.  The insert
-// multiplier 2^(level + 1) = 2^27 >> (nv >> 25) for a refilling lane.
+// so every level update is one multiply-add on the FMA pipe.  A refilling
+// lane inserts its word w as lo += low(w * 2^(level + 1)), hi += high(...),
+// two multiply-adds that carry nowhere (the bits above the valid ones are
+// zero); 2^(level + 1) = 2^27 >> (nv >> 25).
 constexpr int kNvStart = 26 << 25;  // level 0
 
 // Three symbols per ballot round: after a refill a lane holds at least 32 bits,
@@ -201,8 +204,9 @@ constexpr int kNvStart = 26 << 25;  // level 0
 // only by the lanes whose refill came at or before them (predicated loads: the
 // other lanes' entries from the current buffer are already exact), the third
 // by every lane.  Returns the three table entries.
-__device__ __forceinline__ void round3(uint64_t &buf, int &nv, uint32_t &off, uint32_t ring,
-                                       uint32_t tab, uint32_t msk, unsigned lt, uint32_t &e0,
+__device__ __forceinline__ void round3(uint32_t &blo, uint32_t &bhi, int &nv, uint32_t &off,
+                                       uint32_t ring, uint32_t tab, uint32_t msk, unsigned lt,
+                                       uint32_t &e0,
                                        uint32_t &e1, uint32_t &e2) {
   const uint32_t k25 = 1u << 25;
   asm volatile(
@@ -211,17 +215,18 @@ __device__ __forceinline__ void round3(uint64_t &buf, int &nv, uint32_t &off, ui
       ".reg .b32 lo, hi, x, a, t1, t2, b0, b1, b2, mb, bs, c, n2, w, m, s, z;\n\t"
       "mov.b32 z, 0;\n\t"
       "mov.b32 w, 0;\n\t"
-      "mov.b64 {lo, hi}, %0;\n\t"
-      "and.b32 a, lo, %10;\n\t"
-      "or.b32 a, a, %7;\n\t"
-      "ld.shared.u16 %3, [a];\n\t"
-      "shf.r.wrap.b32 x, lo, hi, %3;\n\t"
-      "and.b32 a, x, %10;\n\t"
-      "or.b32 a, a, %7;\n\t"
+      "mov.b32 lo, %0;\n\t"
+      "mov.b32 hi, %1;\n\t"
+      "and.b32 a, lo, %11;\n\t"
+      "or.b32 a, a, %8;\n\t"
       "ld.shared.u16 %4, [a];\n\t"
-      "mad.lo.u32 t1, %3, %9, %1;\n\t"
-      "mad.lo.u32 t2, %4, %9, t1;\n\t"
-      "setp.ge.s32 p0, %1, 603979776;\n\t"
+      "shf.r.wrap.b32 x, lo, hi, %4;\n\t"
+      "and.b32 a, x, %11;\n\t"
+      "or.b32 a, a, %8;\n\t"
+      "ld.shared.u16 %5, [a];\n\t"
+      "mad.lo.u32 t1, %4, %10, %2;\n\t"
+      "mad.lo.u32 t2, %5, %10, t1;\n\t"
+      "setp.ge.s32 p0, %2, 603979776;\n\t"
       "setp.ge.s32 q, t1, 603979776;\n\t"
       "setp.ge.s32 ev, t2, 603979776;\n\t"
       "vote.sync.ballot.b32 b0, p0, 0xffffffff;\n\t"
@@ -231,46 +236,48 @@ __device__ __forceinline__ void round3(uint64_t &buf, int &nv, uint32_t &off, ui
       "selp.b32 bs, b0, bs, p0;\n\t"
       "selp.b32 mb, b0, b1, q;\n\t"
       "selp.b32 mb, 0, mb, p0;\n\t"
-      "lop3.b32 mb, bs, mb, %8, 0xE4;\n\t"
+      "lop3.b32 mb, bs, mb, %9, 0xE4;\n\t"
       "popc.b32 c, mb;\n\t"
-      "mad.lo.u32 a, c, 4, %2;\n\t"
+      "mad.lo.u32 a, c, 4, %3;\n\t"
       "and.b32 a, a, " XP_RING_MASK ";\n\t"
-      "or.b32 a, a, %6;\n\t"
+      "or.b32 a, a, %7;\n\t"
       "@ev ld.shared.u32 w, [a];\n\t"
       "popc.b32 n2, b2;\n\t"
-      "mad.lo.u32 %2, n2, 4, %2;\n\t"
-      "shr.u32 s, %1, 25;\n\t"
+      "mad.lo.u32 %3, n2, 4, %3;\n\t"
+      "shr.u32 s, %2, 25;\n\t"
       "shr.b32 m, 134217728, s;\n\t"
-      "mad.wide.u32 %0, w, m, %0;\n\t"
-      "@ev add.s32 %1, %1, -1073741824;\n\t"
-      "mov.b64 {lo, hi}, %0;\n\t"
-      "and.b32 a, lo, %10;\n\t"
-      "or.b32 a, a, %7;\n\t"
-      "@p0 ld.shared.u16 %3, [a];\n\t"
-      "shf.r.wrap.b32 x, lo, hi, %3;\n\t"
-      "and.b32 a, x, %10;\n\t"
-      "or.b32 a, a, %7;\n\t"
-      "@q ld.shared.u16 %4, [a];\n\t"
-      "shf.r.wrap.b32 x, x, z, %4;\n\t"
-      "and.b32 a, x, %10;\n\t"
-      "or.b32 a, a, %7;\n\t"
-      "ld.shared.u16 %5, [a];\n\t"
-      "add.s32 s, %3, %4;\n\t"
-      "add.s32 s, s, %5;\n\t"
+      "mad.lo.u32 lo, w, m, lo;\n\t"
+      "mad.hi.u32 hi, w, m, hi;\n\t"
+      "@ev add.s32 %2, %2, -1073741824;\n\t"
+      "and.b32 a, lo, %11;\n\t"
+      "or.b32 a, a, %8;\n\t"
+      "@p0 ld.shared.u16 %4, [a];\n\t"
+      "shf.r.wrap.b32 x, lo, hi, %4;\n\t"
+      "and.b32 a, x, %11;\n\t"
+      "or.b32 a, a, %8;\n\t"
+      "@q ld.shared.u16 %5, [a];\n\t"
+      "shf.r.wrap.b32 x, x, z, %5;\n\t"
+      "and.b32 a, x, %11;\n\t"
+      "or.b32 a, a, %8;\n\t"
+      "ld.shared.u16 %6, [a];\n\t"
+      "add.s32 s, %4, %5;\n\t"
+      "add.s32 s, s, %6;\n\t"
       "shf.r.wrap.b32 x, lo, hi, s;\n\t"
       "shf.r.wrap.b32 hi, hi, z, s;\n\t"
-      "mov.b64 %0, {x, hi};\n\t"
-      "mad.lo.u32 %1, s, %9, %1;\n\t"
+      "mov.b32 %0, x;\n\t"
+      "mov.b32 %1, hi;\n\t"
+      "mad.lo.u32 %2, s, %10, %2;\n\t"
       "}"
-      : "+l"(buf), "+r"(nv), "+r"(off), "=&r"(e0), "=&r"(e1), "=&r"(e2)
+      : "+r"(blo), "+r"(bhi), "+r"(nv), "+r"(off), "=&r"(e0), "=&r"(e1), "=&r"(e2)
       : "r"(ring), "r"(tab), "r"(lt), "r"(k25), "r"(msk));
 }
 
 // Two symbols per ballot round, as round3 with one look-ahead entry: a lane
 // refills at symbol i (level < 9) or at i+1 (level - len_i < 9), and the
 // word goes in at most at bit 18.  Returns the two table entries.
-__device__ __forceinline__ void round2(uint64_t &buf, int &nv, uint32_t &off, uint32_t ring,
-                                       uint32_t tab, uint32_t msk, unsigned lt, uint32_t &e0,
+__device__ __forceinline__ void round2(uint32_t &blo, uint32_t &bhi, int &nv, uint32_t &off,
+                                       uint32_t ring, uint32_t tab, uint32_t msk, unsigned lt,
+                                       uint32_t &e0,
                                        uint32_t &e1) {
   const uint32_t k25 = 1u << 25;
   asm volatile(
@@ -279,44 +286,46 @@ __device__ __forceinline__ void round2(uint64_t &buf, int &nv, uint32_t &off, ui
       ".reg .b32 lo, hi, x, a, t1, b0, b1, mb, bs, c, n1, w, m, s, z;\n\t"
       "mov.b32 z, 0;\n\t"
       "mov.b32 w, 0;\n\t"
-      "mov.b64 {lo, hi}, %0;\n\t"
-      "and.b32 a, lo, %9;\n\t"
-      "or.b32 a, a, %6;\n\t"
-      "ld.shared.u16 %3, [a];\n\t"
-      "mad.lo.u32 t1, %3, %8, %1;\n\t"
-      "setp.ge.s32 p0, %1, 603979776;\n\t"
+      "mov.b32 lo, %0;\n\t"
+      "mov.b32 hi, %1;\n\t"
+      "and.b32 a, lo, %10;\n\t"
+      "or.b32 a, a, %7;\n\t"
+      "ld.shared.u16 %4, [a];\n\t"
+      "mad.lo.u32 t1, %4, %9, %2;\n\t"
+      "setp.ge.s32 p0, %2, 603979776;\n\t"
       "setp.ge.s32 ev, t1, 603979776;\n\t"
       "vote.sync.ballot.b32 b0, p0, 0xffffffff;\n\t"
       "vote.sync.ballot.b32 b1, ev, 0xffffffff;\n\t"
       "selp.b32 mb, 0, b0, p0;\n\t"
       "selp.b32 bs, b0, b1, p0;\n\t"
-      "lop3.b32 mb, bs, mb, %7, 0xE4;\n\t"
+      "lop3.b32 mb, bs, mb, %8, 0xE4;\n\t"
       "popc.b32 c, mb;\n\t"
-      "mad.lo.u32 a, c, 4, %2;\n\t"
+      "mad.lo.u32 a, c, 4, %3;\n\t"
       "and.b32 a, a, " XP_RING_MASK ";\n\t"
-      "or.b32 a, a, %5;\n\t"
+      "or.b32 a, a, %6;\n\t"
       "@ev ld.shared.u32 w, [a];\n\t"
       "popc.b32 n1, b1;\n\t"
-      "mad.lo.u32 %2, n1, 4, %2;\n\t"
-      "shr.u32 s, %1, 25;\n\t"
+      "mad.lo.u32 %3, n1, 4, %3;\n\t"
+      "shr.u32 s, %2, 25;\n\t"
       "shr.b32 m, 134217728, s;\n\t"
-      "mad.wide.u32 %0, w, m, %0;\n\t"
-      "@ev add.s32 %1, %1, -1073741824;\n\t"
-      "mov.b64 {lo, hi}, %0;\n\t"
-      "and.b32 a, lo, %9;\n\t"
-      "or.b32 a, a, %6;\n\t"
-      "@p0 ld.shared.u16 %3, [a];\n\t"
-      "shf.r.wrap.b32 x, lo, hi, %3;\n\t"
-      "and.b32 a, x, %9;\n\t"
-      "or.b32 a, a, %6;\n\t"
-      "ld.shared.u16 %4, [a];\n\t"
-      "add.s32 s, %3, %4;\n\t"
+      "mad.lo.u32 lo, w, m, lo;\n\t"
+      "mad.hi.u32 hi, w, m, hi;\n\t"
+      "@ev add.s32 %2, %2, -1073741824;\n\t"
+      "and.b32 a, lo, %10;\n\t"
+      "or.b32 a, a, %7;\n\t"
+      "@p0 ld.shared.u16 %4, [a];\n\t"
+      "shf.r.wrap.b32 x, lo, hi, %4;\n\t"
+      "and.b32 a, x, %10;\n\t"
+      "or.b32 a, a, %7;\n\t"
+      "ld.shared.u16 %5, [a];\n\t"
+      "add.s32 s, %4, %5;\n\t"
       "shf.r.wrap.b32 x, lo, hi, s;\n\t"
       "shf.r.wrap.b32 hi, hi, z, s;\n\t"
-      "mov.b64 %0, {x, hi};\n\t"
-      "mad.lo.u32 %1, s, %8, %1;\n\t"
+      "mov.b32 %0, x;\n\t"
+      "mov.b32 %1, hi;\n\t"
+      "mad.lo.u32 %2, s, %9, %2;\n\t"
       "}"
-      : "+l"(buf), "+r"(nv), "+r"(off), "=&r"(e0), "=&r"(e1)
+      : "+r"(blo), "+r"(bhi), "+r"(nv), "+r"(off), "=&r"(e0), "=&r"(e1)
       : "r"(ring), "r"(tab), "r"(lt), "r"(k25), "r"(msk));
 }
 
@@ -425,7 +434,7 @@ __global__ void __launch_bounds__(kWarps * 32, 10) decode_ring_kernel(const __gr
   bool pending = false;
 
   const unsigned lt = lanemask_lt();
-  uint64_t buf = 0;
+  uint32_t blo = 0, bhi = 0;
   int nv = kNvStart;
   uint32_t off = static_cast<uint32_t>(4 * (a_begin - a0));
   const uint32_t tab = static_cast<uint32_t>(__cvta_generic_to_shared(T));
@@ -446,9 +455,9 @@ __global__ void __launch_bounds__(kWarps * 32, 10) decode_ring_kernel(const __gr
   // (bits 0-2) from there and the exponent (bits 3-6) from the entries.
   auto octet = [&](uint32_t nw, uint32_t &lo, uint32_t &hi) {
     uint32_t e[8];
-    round3(buf, nv, off, base, tab, msk, lt, e[0], e[1], e[2]);
-    round3(buf, nv, off, base, tab, msk, lt, e[3], e[4], e[5]);
-    round2(buf, nv, off, base, tab, msk, lt, e[6], e[7]);
+    round3(blo, bhi, nv, off, base, tab, msk, lt, e[0], e[1], e[2]);
+    round3(blo, bhi, nv, off, base, tab, msk, lt, e[3], e[4], e[5]);
+    round2(blo, bhi, nv, off, base, tab, msk, lt, e[6], e[7]);
     const uint32_t ev = mul_u32(nw & 0x0F0F0F0Fu, 17u);
     const uint32_t od = mul_u32(mulhi_u32(nw, 1u << 28) & 0x0F0F0F0Fu, 17u);
     lo = bitsel(pack4(e[0], e[1], e[2], e[3]), __byte_perm(ev, od, 0x5140), 0x78787878u);
