@@ -265,8 +265,10 @@ int xp_decode_step_noalloc(const void *topk_ids, int ids_bytes, int64_t K, int64
  * not NULL): expand record stg_n[j] (P_n bytes per row) into dst_n[dst_row[e]]
  * (N_n bytes per row) with the LUT lut[e][n] (uint8[E][2][512]), n = 0, 1.
  * chunk: values per lane (512 in production; multiple of 8, at most 2^30; N_n
- * a multiple of 32*chunk).  Records are in the reference's format
- * (codec.py:22-26). */
+ * a multiple of 32*chunk).  stg_n and dst_n start on 16-byte boundaries and P_n
+ * is a multiple of 16 (else XP_EINVAL); rows on 32-byte boundaries with chunk a
+ * multiple of 32 are written with 32-byte stores.  Records are in the
+ * reference's format (codec.py:22-26). */
 int xp_decode_rows(const int64_t *todo, int64_t K, const int64_t *dst_row,
                    const int64_t *cache_row, const uint8_t *lut,
                    const void *stg0, int64_t P0, void *dst0, int64_t N0,
