@@ -158,7 +158,7 @@ __device__ __forceinline__ uint32_t bitsel(uint32_t a, uint32_t b, uint32_t m) {
 // (offset & 2047) | base with a 2 KiB-aligned base, so no read leaves the ring
 // whatever the record holds: a corrupt record can only decode to wrong bytes.
 constexpr uint32_t kRing = 2048, kHalf = 1024;
-#define XP_RING_MASK "2047"  // kRing - 1, spelled for the step functions' PTX
+#define XP_RING_MASK "2047"  // kRing - 1, spelled for the round functions' PTX
 static_assert(kRing == 2048, "XP_RING_MASK spells kRing - 1");
 // Most stream bytes a valid record's refills consume in 16 symbols: a lane
 // refills at most once every 3 symbols, so 6 words per lane.
