@@ -419,6 +419,8 @@ class PagedMoE:
                         src = recs[int(a[e]), n] if compress else \
                             pw[n][0][int(a[e])].view(torch.int32).reshape(-1).cpu()
                         blob[e, off : off + store.pitch[n]] = src.view(torch.uint8)
+                        if compress:
+                            store.mark_used(layer, e, n, src)
                 os.pwrite(store.fd_w, memoryview(blob.numpy()), layer * E * store.record_bytes)
         if store.fd_w is not None:
             os.fsync(store.fd_w)
@@ -570,7 +572,7 @@ def model_decode(m, device, batch: int, tokens: int, h2d_peak: float | None = No
         graph.replay()
     torch.cuda.synchronize()
     store = m.store
-    miss0, reads0 = m.misses(), store.reads
+    miss0, reads0, bytes0 = m.misses(), store.reads, store.bytes_read
     gu0 = int(store.req[store.giveup_at])
 
     def run():
@@ -582,19 +584,20 @@ def model_decode(m, device, batch: int, tokens: int, h2d_peak: float | None = No
         ms = timed(run)
     misses = m.misses() - miss0
     reads = store.reads - reads0
+    disk_bytes = store.bytes_read - bytes0
     finite = bool(torch.isfinite(y).all())
     del graph
     m.check()
-    record = store.record_bytes if store.compress else EXPERT_BYTES
-    # The fused step copies a compressed record's used words only (its header says
-    # how many); the working path's gather copies whole records.
+    # The fused step and the working path's gather copy a compressed record's used
+    # words only (its header says how many).
     step_bytes = m.used_mean if store.compress else EXPERT_BYTES
     res = {"layers": m.L, "batch": batch, "tokens": tokens, "ms": round(ms, 2),
            "tok_per_s": round(tokens * batch / (ms * 1e-3), 2),
            "tpot_ms": round(ms / tokens, 3),
            "path": "decode (fused step)" if batch * TOPK <= m.S else "working slab (chunks)",
            "ssd_reads": reads,
-           "ssd_gb_per_s": round(reads * record / (ms * 1e-3) / 1e9, 3),
+           "ssd_gb_per_s": round(disk_bytes / (ms * 1e-3) / 1e9, 3),
+           "ssd_bytes_per_read": round(disk_bytes / reads) if reads else None,
            "ssd_failed": store.failed,
            "giveups": int(store.req[store.giveup_at]) - gu0,
            "step_errors": sum(p.step_errors() for p in m.pagers),
@@ -652,14 +655,16 @@ def model_decode(m, device, batch: int, tokens: int, h2d_peak: float | None = No
         probe_res["host_link"] = link
     if ev["copy"]:
         c_ms, c_rows, c_n = _sum_events(ev["copy"])
-        ach = c_rows * record / (c_ms * 1e-3) / 1e9 if c_ms > 0 else 0.0
+        ach = c_rows * step_bytes / (c_ms * 1e-3) / 1e9 if c_ms > 0 else 0.0
         link = {"kernel": "gather_kernel (working path: RAM tier -> staging)",
                 "bound": "host_link", "launches": c_n, "rows": c_rows, "unit": "GB/s",
-                "achieved": round(ach, 3)}
+                "achieved": round(ach, 3),
+                "how": "rows copied from the RAM tier x bytes per row (compressed: the "
+                       "records' used bytes, mean over the pool) / gather_kernel time"}
         if h2d_peak:
             link.update({"peak": round(h2d_peak, 3), "frac": round(ach / h2d_peak, 4)})
         probe_res["host_link"] = link
-        res["paged_gb_per_s"] = round(c_rows * record / (probe * batch) * res["tok_per_s"]
+        res["paged_gb_per_s"] = round(c_rows * step_bytes / (probe * batch) * res["tok_per_s"]
                                       / 1e9, 3)
         res["paged_gb_per_s_how"] = "record bytes per token of the probe steps x timed tok/s"
     res["probe"] = probe_res
@@ -716,10 +721,11 @@ def run_prefill(args, device, path) -> dict:
 
             layer_paged(0)  # warm-up (JIT)
             torch.cuda.synchronize()
-            reads0 = m.store.reads
+            reads0, bytes0 = m.store.reads, m.store.bytes_read
             with Clocks(torch.cuda.current_device()) as clocks:
                 ms = timed(lambda: [layer_paged(l) for l in range(args.layers)])
             reads = m.store.reads - reads0
+            disk_bytes = m.store.bytes_read - bytes0
             # MoE alone on resident weights (the pool), for the overlap fraction.
             pw = m.pool_weights
             pool_ids = (ids % pw["w13_weight"][0].shape[0]).to(torch.int32)
@@ -729,7 +735,8 @@ def run_prefill(args, device, path) -> dict:
                 torch.empty_like(h)) for _ in range(args.layers)])
             res["overlap" if overlap else "serial"] = {
                 "ms_per_layer": round(ms / args.layers, 3), "ssd_reads": reads,
-                "ssd_gb_per_s": round(reads * m.store.record_bytes / (ms * 1e-3) / 1e9, 3),
+                "ssd_gb_per_s": round(disk_bytes / (ms * 1e-3) / 1e9, 3),
+                "ssd_bytes_per_read": round(disk_bytes / reads) if reads else None,
                 "moe_only_ms_per_layer": round(moe_ms / args.layers, 3),
                 "clocks": clocks.summary()}
         res["giveups"] = int(m.store.req[m.store.giveup_at])

@@ -124,6 +124,10 @@ int xp_plan_working(const void *ids, int ids_bytes, int64_t K, int64_t E, int64_
  *   else:              src_n[src_row[e]+base] (P_n == W_n) -> dst_n[dst_row[e]];
  * and always scale_n[e] (SW_n words) -> sdst_n[dst_row[e]], for names n = 0, 1.
  * src_n may be pinned host memory (read over the host link by the SMs).
+ * chunk (compressed rows only; not in the reference): the records' values per
+ * lane; when > 0 (and at most 64 entries are copied from the RAM tier) only each
+ * record's used words -- header, nibbles, Huffman words, read from its header --
+ * cross the host link, as in xp_decode_step; 0 copies whole P_n-word records.
  * ctas: copying CTAs (0 = default).  If req is not NULL, one more CTA runs
  * xp_fetch on skip (the decode path's fused publish + wait, gather.py:170-185);
  * its arguments are those of xp_fetch. */
@@ -135,7 +139,7 @@ int xp_gather_rows(const int64_t *todo, int64_t K, const int64_t *dst_row,
                    int64_t P1,
                    const void *scale0, void *sdst0, int64_t SW0,
                    const void *scale1, void *sdst1, int64_t SW1,
-                   const int64_t *skip, int compress, int ctas,
+                   const int64_t *skip, int compress, int64_t chunk, int ctas,
                    int64_t layer, int64_t *seq, int64_t *req, const int64_t *done,
                    int64_t block, int64_t ring, int64_t retry_ns, int64_t giveup,
                    void *stream);
@@ -329,6 +333,16 @@ int ssd_numa_node(void *server);
  * server's threads concurrently.  A request of one or two experts then keeps
  * nworkers+1 reads in flight instead of one or two. */
 void ssd_set_read_chunk(void *server, long bytes);
+/* No counterpart in the reference: used[(layer*E + e)*names + i] gives the
+ * bytes of name i's piece of record (layer, e) that hold data (for compressed
+ * records: header, nibbles and Huffman words; 0, or at least the piece's
+ * pitch: the whole piece).  Later requests read each piece only up to its last
+ * data page, so the disk moves ~8 % fewer bytes per compressed record; the
+ * rest of the RAM-tier row keeps old bytes, which the decoder never reads.
+ * The array is the caller's and must outlive the server (NULL: whole records). */
+void ssd_set_used_bytes(void *server, const long *used);
+/* No counterpart in the reference: bytes the server has read from the file. */
+long ssd_bytes_read(void *server);
 
 #ifdef __cplusplus
 }

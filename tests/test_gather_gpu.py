@@ -86,7 +86,7 @@ def test_raw_rows_from_pinned_memory(words):
             _ptr(source[1]), cache[1].data_ptr(), dst[1].data_ptr(), None, words[1], words[1],
             scale[0].data_ptr(), scale_dst[0].data_ptr(), 8,
             scale[1].data_ptr(), scale_dst[1].data_ptr(), 8,
-            skip.data_ptr(), 0, 8, 0, None, None, None, 0, 0, 0, 0,
+            skip.data_ptr(), 0, 0, 8, 0, None, None, None, 0, 0, 0, 0,
             torch.cuda.current_stream().cuda_stream), "gather")
         torch.cuda.synchronize()
         for i in range(2):

@@ -378,3 +378,63 @@ def test_pipelined_requests_finish_in_order(tmp_path):
         assert r.error() is None and r.stats()[:2] == (6, 6 * 24)
     finally:
         r.close()
+
+
+@pytest.mark.parametrize("chunk", [0, 4096, 8192])
+def test_used_bytes_reads_only_the_data_pages(tmp_path, chunk):
+    """ssd_set_used_bytes: each record piece is read only up to the page holding its
+    last used byte (0 or a length of the whole pitch or more reads the whole piece);
+    the rest of the RAM-tier row keeps its old bytes, and ssd_bytes_read counts the
+    bytes read."""
+    so = native.lib()
+    L, E, R = 2, 8, 4
+    pitch = (12288, 8192)
+    r = Ring(so, tmp_path, L=L, E=E, R=R, pitch=pitch)
+    try:
+        so.ssd_set_read_chunk(ctypes.c_void_p(r.h), chunk)
+        rng = np.random.default_rng(chunk + 1)
+        used = np.zeros(L * E * 2, dtype=np.int64)
+        for i in range(L * E):
+            used[2 * i] = [0, 1, 4096, 4097, 9000, 12288, 20000][i % 7]
+            used[2 * i + 1] = [100, 8192, 0, 4096, 5000][i % 5]
+        so.ssd_set_used_bytes(ctypes.c_void_p(r.h), ctypes.c_void_p(used.ctypes.data))
+        for k in range(2):
+            r.pinned[k][:] = 0xEE
+        want_bytes = 0
+        for step in range(6):
+            layer = int(rng.integers(0, L))
+            experts = rng.choice(E, 3, replace=False).tolist()
+            rows = [3 * step % (L * R), 3 * step % (L * R) + 1, 3 * step % (L * R) + 2]
+            for k in range(2):
+                for row in rows:
+                    r.row(k, row)[:] = 0xEE
+            r.wait(r.publish(layer, experts, rows))
+            for e, row in zip(experts, rows):
+                for k in range(2):
+                    u = int(used[2 * (layer * E + e) + k])
+                    n = pitch[k] if u <= 0 or u >= pitch[k] else -(-u // 4096) * 4096
+                    got, want = r.row(k, row), r.expected(k, layer, e)
+                    assert np.array_equal(got[:n], want[:n]), (e, k, n)
+                    assert np.all(got[n:] == 0xEE), (e, k, n)
+                    want_bytes += n
+        assert r.error() is None
+        assert so.ssd_bytes_read(ctypes.c_void_p(r.h)) == want_bytes
+    finally:
+        r.close()
+
+
+def test_used_bytes_null_reads_whole_records(tmp_path):
+    """ssd_set_used_bytes(NULL) restores whole-record reads."""
+    so = native.lib()
+    r = Ring(so, tmp_path, L=1, E=4, R=2, pitch=(8192, 4096))
+    try:
+        used = np.full(8, 1, dtype=np.int64)
+        so.ssd_set_used_bytes(ctypes.c_void_p(r.h), ctypes.c_void_p(used.ctypes.data))
+        so.ssd_set_used_bytes(ctypes.c_void_p(r.h), None)
+        r.wait(r.publish(0, [1, 2], [0, 1]))
+        for e, row in ((1, 0), (2, 1)):
+            for k in range(2):
+                assert np.array_equal(r.row(k, row), r.expected(k, 0, e))
+        assert so.ssd_bytes_read(ctypes.c_void_p(r.h)) == 2 * (8192 + 4096)
+    finally:
+        r.close()

@@ -90,7 +90,8 @@ extern "C" int xp_gather_rows(const int64_t *todo, int64_t K, const int64_t *dst
                               int64_t W0, int64_t P0, const void *src1, const void *cache1,
                               void *dst1, void *stg1, int64_t W1, int64_t P1, const void *scale0,
                               void *sdst0, int64_t SW0, const void *scale1, void *sdst1,
-                              int64_t SW1, const int64_t *skip, int compress, int ctas,
+                              int64_t SW1, const int64_t *skip, int compress, int64_t chunk,
+                              int ctas,
                               int64_t layer, int64_t *seq, int64_t *req, const int64_t *done,
                               int64_t block, int64_t ring, int64_t retry_ns, int64_t giveup,
                               void *stream) {
@@ -112,6 +113,16 @@ extern "C" int xp_gather_rows(const int64_t *todo, int64_t K, const int64_t *dst
   bool vec;
   if (!fill_names(a.job, srcs, caches, dsts, stgs, Ws, Ps, scales, sdsts, SWs, compress, vec))
     return XP_EINVAL;
+  // Compressed rows with a known record layout: copy only each record's used words.
+  if (chunk < 0) return XP_EINVAL;
+  if (compress && chunk > 0) {
+    if (chunk % 8) return XP_EINVAL;
+    for (int i = 0; i < 2; ++i) {
+      const int64_t N = 4 * Ws[i];  // raw bytes of a row
+      if (N <= 0 || N % (32 * chunk)) return XP_EINVAL;
+      a.job.groups[i] = N / (32 * chunk);
+    }
+  }
   if (ctas < 0 || ctas > XP_MAX_COPY_CTAS) return XP_EINVAL;
   a.copy_ctas = ctas > 0 ? ctas : kDefaultCtas;
   a.fetch = req != nullptr;

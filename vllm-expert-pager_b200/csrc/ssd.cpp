@@ -134,6 +134,10 @@ struct Server {
   std::atomic<int> failing{0}, failed{0};
   std::atomic<double> test_delay{0.0};
   std::atomic<long> read_chunk{0};  // bytes per job, 0: whole records
+  // Optional: the bytes of each record piece that hold data, used[(layer*E +
+  // e)*names + i] (0 or more than the pitch: the whole piece); caller-owned.
+  std::atomic<const long *> used{nullptr};
+  std::atomic<long> bytes_read{0};
 
   // A job: bytes [lo, hi) of one record, read into that record's row; tag is
   // the slot of its request in the ring of kPipeline requests in flight.
@@ -191,6 +195,7 @@ struct Server {
     }
     const off_t off = static_cast<off_t>(layer * E + e) * record_bytes + jb.lo;
     ssize_t n = preadv(fd, iov, k, off);
+    if (n > 0) bytes_read.fetch_add(static_cast<long>(n), std::memory_order_relaxed);
     if (n < 0)
       fail("preadv of expert %ld of layer %ld failed: %s", e, layer, strerror(errno));
     else if (n != jb.hi - jb.lo)
@@ -247,14 +252,30 @@ struct Server {
       jobs.clear();
       next = 0;
     }
+    // With used lengths (records laid out as the names' pieces), each piece is
+    // read only up to its last data page: the decoder never looks past a
+    // record's used words.
+    const long *u = sum == record_bytes ? used.load(std::memory_order_acquire) : nullptr;
     long n = 0, nj = 0;
     for (long j = 0; j < block; ++j) {
       const int64_t e = slot[2 + j];
       if (e < 0) continue;
       const long row = static_cast<long>(slot[2 + block + j]);
-      for (long lo = 0; lo < record_bytes; lo += c, ++nj)
-        jobs.push_back(Job{layer, static_cast<long>(e), row, lo,
-                           lo + c < record_bytes ? lo + c : record_bytes, tag});
+      const bool in_range = layer >= 0 && layer < L && e >= 0 && e < E;
+      long base = 0;
+      for (int i = 0; i < (u && in_range ? names : 1); ++i) {
+        long lo0 = 0, hi0 = record_bytes;
+        if (u && in_range) {
+          long len = u[(layer * E + e) * names + i];
+          len = len <= 0 || len >= pitch[i] ? pitch[i] : (len + 4095) / 4096 * 4096;
+          lo0 = base;
+          hi0 = base + (len < pitch[i] ? len : pitch[i]);
+          base += pitch[i];
+        }
+        for (long lo = lo0; lo < hi0; lo += c, ++nj)
+          jobs.push_back(Job{layer, static_cast<long>(e), row, lo, lo + c < hi0 ? lo + c : hi0,
+                             tag});
+      }
       ++n;
     }
     f.experts = n;
@@ -413,6 +434,16 @@ extern "C" const char *ssd_error(void *server) {
 extern "C" void ssd_set_read_chunk(void *server, long bytes) {
   if (!server) return;
   static_cast<Server *>(server)->read_chunk.store(bytes < 0 ? 0 : bytes, std::memory_order_relaxed);
+}
+
+extern "C" void ssd_set_used_bytes(void *server, const long *used) {
+  if (!server) return;
+  static_cast<Server *>(server)->used.store(used, std::memory_order_release);
+}
+
+extern "C" long ssd_bytes_read(void *server) {
+  if (!server) return 0;
+  return static_cast<Server *>(server)->bytes_read.load(std::memory_order_relaxed);
 }
 
 extern "C" void ssd_test_delay(void *server, double seconds) {

@@ -57,6 +57,7 @@ def gather_rows(
     scale_dst: list[torch.Tensor],
     fetch: tuple[torch.Tensor, int, object] | None = None,
     ctas: int | None = None,
+    chunk: int = 0,
 ) -> None:
     """Copy the rows and scales of the experts in ``todo`` (gather.py:328-393).
 
@@ -71,6 +72,11 @@ def gather_rows(
     With ``fetch=(ssd_todo, layer, store)`` one more CTA of the same launch asks
     the host to read ``ssd_todo`` from SSD and waits, while the copy skips those
     experts; a later ``gather_rows(ssd_todo, ...)`` copies them.
+
+    ``chunk`` (not in the reference): with compressed rows, the records' values
+    per lane; when > 0, only each record's used words (header, nibbles, Huffman
+    words) are copied from the RAM tier, the rest of its staging row is left as
+    it was (the decoder never reads it).  0 copies whole records.
     """
     W0, W1 = dst[0].shape[1], dst[1].shape[1]
     P0, P1 = src[0].shape[1], src[1].shape[1]
@@ -102,7 +108,7 @@ def gather_rows(
             _src_ptr(src[1]), cache[1].data_ptr(), dst[1].data_ptr(), native.ptr(st[1]), W1, P1,
             scale[0].data_ptr(), scale_dst[0].data_ptr(), scale[0].shape[1],
             scale[1].data_ptr(), scale_dst[1].data_ptr(), scale[1].shape[1],
-            native.ptr(ssd), int(compress), ctas or GATHER_CTAS,
+            native.ptr(ssd), int(compress), int(chunk) if compress else 0, ctas or GATHER_CTAS,
             layer, seq, req, done, block, ring, retry, giveup,
             native.stream_of(device),
         ),

@@ -39,7 +39,7 @@ _SIGNATURES = {
                               _p, _p, _p, _p, _i64, _i64,
                               _p, _p, _p, _p, _i64, _i64,
                               _p, _p, _i64, _p, _p, _i64,
-                              _p, _i32, _i32,
+                              _p, _i32, _i64, _i32,
                               _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p]),
     "xp_fetch_publish": (_i32, [_p, _i64, _p, _i64, _i64, _p, _p, _p, _i64, _i64, _p]),
     "xp_fetch_wait": (_i32, [_p, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p]),
@@ -79,6 +79,8 @@ _SIGNATURES = {
     "ssd_test_delay": (None, [_p, ctypes.c_double]),
     "ssd_numa_node": (_i32, [_p]),
     "ssd_set_read_chunk": (None, [_p, _long]),
+    "ssd_set_used_bytes": (None, [_p, _p]),
+    "ssd_bytes_read": (_long, [_p]),
 }
 
 XP_OK = 0

@@ -315,7 +315,8 @@ class LayerPager:
             ev = timing(copy_events)
             if ev:
                 ev[0].record()
-            gather_rows(part, dst_row, cached_row, src_row, 0, *rows(h))
+            gather_rows(part, dst_row, cached_row, src_row, 0, *rows(h),
+                        chunk=codec.CHUNK if store.compress else 0)
             if ev:
                 ev[1].record()
                 copy_events.append((*ev, n))

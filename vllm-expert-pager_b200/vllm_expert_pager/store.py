@@ -14,7 +14,9 @@ request ring and statistics.  What changed:
   reference's C server: ssd_start/ssd_stop/ssd_stats/ssd_error/ssd_test_delay),
   which also splits each record read into page-aligned jobs read by all its
   threads at once (``VLLM_EXPERT_PAGER_READ_CHUNK``, 512 KiB; 0 reads whole
-  records as the reference does).
+  records as the reference does), and reads a compressed record only up to the
+  last page of each name's used words (``VLLM_EXPERT_PAGER_READ_USED``, on; the
+  decoder never reads past them), ~8 % fewer disk bytes per record.
 * The GPU's wait for the host is bounded by time: ``retry_ns`` between
   re-publishes and ``giveup`` re-publishes (settable per store).
 
@@ -52,6 +54,9 @@ _READ_WORKERS = max(1, int(os.environ.get("VLLM_EXPERT_PAGER_READ_WORKERS", "8")
 # request of one or two experts keeps all of them busy.  0 reads whole records,
 # one per thread, as the reference does.  VLLM_EXPERT_PAGER_READ_CHUNK sets it.
 _READ_CHUNK = max(0, int(os.environ.get("VLLM_EXPERT_PAGER_READ_CHUNK", str(512 << 10))))
+# Compressed records are read only up to the last page of each name's used
+# words (header, nibbles, Huffman words); 0 reads whole records.
+_READ_USED = os.environ.get("VLLM_EXPERT_PAGER_READ_USED", "1") != "0"
 # Slots in the request ring (store.py:65-67).
 RING = 4
 # GPU wait for the host: re-publish every RETRY_NS, give up after GIVEUP
@@ -231,6 +236,11 @@ class Store:
         if not self._handle:
             raise RuntimeError("vllm-expert-pager: cannot start the SSD server")
         self._so.ssd_set_read_chunk(ctypes.c_void_p(self._handle), _READ_CHUNK)
+        # Used bytes of each record piece, filled by write(); 0 = the whole piece.
+        self._used = np.zeros(self.num_layers * self.num_experts * n, dtype=np.int64)
+        if self.compress and _READ_USED:
+            self._so.ssd_set_used_bytes(ctypes.c_void_p(self._handle),
+                                        ctypes.c_void_p(self._used.ctypes.data))
 
     def close(self) -> None:
         """Stop the host server and release the pinned memory and files."""
@@ -260,6 +270,19 @@ class Store:
         """For tests: delay the host between seeing a request and serving it."""
         self._so.ssd_test_delay(ctypes.c_void_p(self._handle), seconds)
 
+    def mark_used(self, layer: int, expert: int, name: str, record) -> None:
+        """Note how many bytes of a compressed record written to the paging file hold
+        data (header G + 1 words, nibbles N / 8 words, then header[G] Huffman words),
+        so that the host server reads it only up to that page.  ``write`` calls it;
+        a caller that writes records to the paging file itself calls it per record
+        (``record``: the record's int32 words on the host)."""
+        if getattr(self, "_used", None) is None:
+            return
+        G = self.row_bytes[name] // codec.GROUP
+        used = 4 * (G + 1 + self.row_bytes[name] // 8 + max(int(record[G]), 0))
+        k = (layer * self.num_experts + expert) * len(self.names) + self.names.index(name)
+        self._used[k] = min(used, self.pitch[name])
+
     # ---- statistics (written by the host server) ----
 
     def _stats(self) -> tuple[int, int, float, int]:
@@ -285,6 +308,11 @@ class Store:
     def io_seconds(self) -> float:
         """Total time from seeing a request to writing done."""
         return self._stats()[2]
+
+    @property
+    def bytes_read(self) -> int:
+        """Bytes the host server has read from the paging file."""
+        return int(self._so.ssd_bytes_read(ctypes.c_void_p(self._handle))) if self._handle else 0
 
     @property
     def missed(self) -> int:
@@ -336,4 +364,7 @@ class Store:
             self.pinned[name][layer * self.ram_slots + expert].copy_(words)
         if self.fd_w is not None:
             offset = (layer * self.num_experts + expert) * self.record_bytes + self.offset[name]
-            os.pwrite(self.fd_w, memoryview(np.ascontiguousarray(words.cpu().numpy())), offset)
+            host = np.ascontiguousarray(words.cpu().numpy())
+            os.pwrite(self.fd_w, memoryview(host), offset)
+            if self.compress:
+                self.mark_used(layer, expert, name, host)
