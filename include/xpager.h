@@ -337,7 +337,8 @@ void ssd_set_read_chunk(void *server, long bytes);
  * bytes of name i's piece of record (layer, e) that hold data (for compressed
  * records: header, nibbles and Huffman words; 0, or at least the piece's
  * pitch: the whole piece).  Later requests read each piece only up to its last
- * data page, so the disk moves ~8 % fewer bytes per compressed record; the
+ * data page (when every pitch is a whole number of 4 KiB pages, as Store's are;
+ * else whole records), so the disk moves ~7 % fewer bytes per compressed record; the
  * rest of the RAM-tier row keeps old bytes, which the decoder never reads.
  * The array is the caller's and must outlive the server (NULL: whole records). */
 void ssd_set_used_bytes(void *server, const long *used);

@@ -246,7 +246,11 @@ struct Server {
     // exactly the names' pieces (always, for records written by Store).
     long c = read_chunk.load(std::memory_order_relaxed) / 4096 * 4096;
     long sum = 0;
-    for (int i = 0; i < names; ++i) sum += pitch[i];
+    bool paged = true;  // every piece starts on a page (O_DIRECT offsets)
+    for (int i = 0; i < names; ++i) {
+      sum += pitch[i];
+      paged = paged && pitch[i] % 4096 == 0;
+    }
     if (c <= 0 || c >= record_bytes || sum != record_bytes) c = record_bytes;
     if (next >= static_cast<long>(jobs.size())) {  // every queued job taken: start afresh
       jobs.clear();
@@ -255,7 +259,7 @@ struct Server {
     // With used lengths (records laid out as the names' pieces), each piece is
     // read only up to its last data page: the decoder never looks past a
     // record's used words.
-    const long *u = sum == record_bytes ? used.load(std::memory_order_acquire) : nullptr;
+    const long *u = sum == record_bytes && paged ? used.load(std::memory_order_acquire) : nullptr;
     long n = 0, nj = 0;
     for (long j = 0; j < block; ++j) {
       const int64_t e = slot[2 + j];
