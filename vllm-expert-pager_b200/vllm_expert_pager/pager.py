@@ -125,6 +125,9 @@ class LayerPager:
             self.decode_staging = [flat[n][: need[n]].view(S, store.pitch[n]) for n in PARAMS]
         self.ram_view = [store.view[n] for n in PARAMS]
         self.side = torch.cuda.Stream(device=device)
+        # The working path's decodes: beside the copies, so that chunk k's decode
+        # does not hold back chunk k+1's copy over the host link.
+        self.expand_side = torch.cuda.Stream(device=device)
         # Flags of the fused decode step (zero between launches; word 3 counts
         # waits that gave up).
         self.step_scratch = torch.zeros((4,), dtype=torch.int32, device=device)
@@ -294,6 +297,7 @@ class LayerPager:
         staging = self.working.staging
         main = torch.cuda.current_stream(store.device)
         side = self.side if overlap else main
+        dec = self.expand_side if overlap else main
 
         def rows(h):
             wr = self.working_rows[h]
@@ -307,11 +311,13 @@ class LayerPager:
                 return None
             return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
+        def rows_read(part):
+            if decode_events is None and copy_events is None:
+                return None
+            # Entries not in the cache slab: read from the RAM tier, and expanded.
+            return ((part >= 0) & (cached_row[part.clamp(min=0)] < 0)).sum()
+
         def copy(part, h):
-            n = None
-            if decode_events is not None or copy_events is not None:
-                # Entries not in the cache slab: read from the RAM tier, and expanded.
-                n = ((part >= 0) & (cached_row[part.clamp(min=0)] < 0)).sum()
             ev = timing(copy_events)
             if ev:
                 ev[0].record()
@@ -319,16 +325,17 @@ class LayerPager:
                         chunk=codec.CHUNK if store.compress else 0)
             if ev:
                 ev[1].record()
-                copy_events.append((*ev, n))
-            if store.compress:
-                stg = [t[h * W : (h + 1) * W] for t in staging]
-                ev = timing(decode_events)
-                if ev:
-                    ev[0].record()
-                codec.decode_rows(part, dst_row, cached_row, stg, self.working_bytes[h], lut)
-                if ev:
-                    ev[1].record()
-                    decode_events.append((*ev, n))
+                copy_events.append((*ev, rows_read(part)))
+
+        def expand(part, h):
+            stg = [t[h * W : (h + 1) * W] for t in staging]
+            ev = timing(decode_events)
+            if ev:
+                ev[0].record()
+            codec.decode_rows(part, dst_row, cached_row, stg, self.working_bytes[h], lut)
+            if ev:
+                ev[1].record()
+                decode_events.append((*ev, rows_read(part)))
 
         def chunk(t, k):
             return t[k * W : (k + 1) * W]
@@ -338,6 +345,13 @@ class LayerPager:
 
         copied = [torch.cuda.Event() for _ in range(N)]
         consumed = [torch.cuda.Event() for _ in range(N)]
+        # Compressed rows: chunk k's RAM rows are expanded on the decode stream while
+        # the copy stream goes on with the SSD wait, the SSD rows and chunk k+1's
+        # copies (into the other staging half).  A half's staging and slab rows are
+        # reused two chunks later, after the MoE that read them (consumed), which
+        # itself waited for their decode (copied).
+        early = [torch.cuda.Event() for _ in range(N)]
+        gathered = [torch.cuda.Event() for _ in range(N)]
         out = None
         side.wait_stream(main)  # the plan is on the main stream
         with torch.cuda.stream(side):
@@ -348,11 +362,21 @@ class LayerPager:
                 if k >= halves:
                     side.wait_event(consumed[k - halves])  # the half's previous MoE is done
                 copy(chunk(todo, k), h)
+                early[k].record(side)
                 if k + 1 < N:
                     fetch_publish_rows(chunk(ssd, k + 1), src_row, 0, layer, store, ticket(k + 1))
                 fetch_wait_rows(chunk(ssd, k), store, ticket(k))
                 copy(chunk(late, k), h)
-                copied[k].record(side)
+                gathered[k].record(side)
+            if store.compress:
+                with torch.cuda.stream(dec):
+                    dec.wait_event(early[k])
+                    expand(chunk(todo, k), h)
+                    dec.wait_event(gathered[k])
+                    expand(chunk(late, k), h)
+                    copied[k].record(dec)
+            else:
+                copied[k] = gathered[k]
             main.wait_event(copied[k])
             self.expert_map.copy_(maps[k])
             out = run_chunk(k, N, self.working.half(h), self.expert_map)
