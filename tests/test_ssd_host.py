@@ -330,7 +330,10 @@ def test_pipelined_requests_finish_in_order(tmp_path):
     working path does): this server reads them with up to two in flight, and done
     still only moves in seq order, each value after all of that request's rows landed.
     A watcher thread records every done value it sees and checks, at that moment,
-    that the rows of every request up to it hold their records."""
+    that the rows of every request up to it hold their records.  Requests alternate
+    between two faces of rows, and request q+2 (which overwrites request q's face) is
+    published only after the watcher has checked request q, as the working path reuses
+    a face only after its MoE has read it."""
     import threading
 
     r = Ring(native.lib(), tmp_path, L=2, E=64, R=8, working=128, workers=7,
@@ -339,6 +342,7 @@ def test_pipelined_requests_finish_in_order(tmp_path):
     try:
         seen, bad = [], []
         reqs = {}
+        checked = {q: threading.Event() for q in range(1, 7)}
 
         def watch():
             last = 0
@@ -353,6 +357,7 @@ def test_pipelined_requests_finish_in_order(tmp_path):
                             for k in (0, 1):
                                 if not np.array_equal(r.row(k, row), r.expected(k, layer, e)):
                                     bad.append((q, e, k))
+                        checked[q].set()
                     last = d
                 time.sleep(0.0001)
 
@@ -369,6 +374,8 @@ def test_pipelined_requests_finish_in_order(tmp_path):
         # publish k+1 before waiting for k (two in flight), as the working path does
         r.publish(*plan[0])
         for q in range(2, 7):
+            if q >= 3:
+                assert checked[q - 2].wait(20), f"request {q - 2} never checked"
             r.publish(*plan[q - 1])
             r.wait(q - 1)
         r.wait(6)
