@@ -35,7 +35,7 @@ def _rank(rank, world, port, out):
 def test_replica_aggregation_over_gloo():
     world = 2
     port = 29600 + os.getpid() % 200
-    with mp.Manager() as m:
+    with mp.get_context("spawn").Manager() as m:  # no fork of a threaded process
         out = m.dict()
         mp.spawn(_rank, args=(world, port, out), nprocs=world, join=True)
         res = dict(out)
