@@ -193,3 +193,57 @@ def test_decode_rejects_bad_shapes():
     lut = torch.zeros((1, 2, 512), dtype=torch.uint8, device=DEV)
     with pytest.raises(ValueError):
         codec.decode_rows(t, t, t, stg, dst, lut, chunk=64)
+
+
+@pytest.mark.parametrize("chunk", [512, 40], ids=["ring", "window"])
+def test_corrupt_records_stay_inside_their_rows(chunk):
+    """A corrupt record decodes to wrong bytes and nothing else: its group offsets are
+    clamped to the record, its ring and table addresses are masked, and every store goes
+    to its own destination row.  Staging rows of random bytes whose headers hold random,
+    decreasing, zero and past-the-record offsets leave the canary rows around their
+    destinations untouched, and a valid decode right after is exact.  LUTs stay valid
+    (codes of at most 9 bits); the ring path (chunk 512) also takes a random LUT."""
+    from vllm_expert_pager import codec
+
+    rng = np.random.default_rng(chunk)
+    E, groups = 4, 4
+    N = groups * 32 * chunk
+    ns = (N, N // 2) if chunk == 512 else (N, N)
+    pitches = [codec.pitch_of(n, 1.25, 4096) for n in ns]
+    raws = {e: [rows(40 + 2 * e + k, n) for k, n in enumerate(ns)] for e in range(E)}
+    good = [torch.zeros((E, p), dtype=torch.uint8, device=DEV) for p in pitches]
+    lut = torch.zeros((E, 2, codec.LUT_BYTES), dtype=torch.uint8, device=DEV)
+    for e in range(E):
+        for k in range(2):
+            good[k][e], lut[e, k] = codec.encode(raws[e][k].to(DEV), pitches[k], chunk)
+    bad = []
+    for k, (n, p) in enumerate(zip(ns, pitches)):
+        b = rng.integers(0, 256, (E, p), dtype=np.uint8)
+        G = n // (32 * chunk)
+        hdr = b[:, : 4 * (G + 1)].view(np.int32)
+        hdr[0] = rng.integers(-(2**31), 2**31 - 1, G + 1)  # anything
+        hdr[1] = np.linspace(2**31 - 1, -(2**20), G + 1).astype(np.int32)  # decreasing
+        hdr[2] = 0  # every group empty: the ring is never filled
+        hdr[3] = np.arange(G + 1, dtype=np.int32) * (p // 4) + p  # past the record
+        bad.append(torch.from_numpy(b).to(DEV))
+    todo = torch.arange(E, dtype=torch.int64, device=DEV)
+    dst_row = torch.arange(1, E + 1, dtype=torch.int64, device=DEV)  # rows 0 and E+1: canaries
+    cache_row = torch.full((E,), -1, dtype=torch.int64, device=DEV)
+    dst = [torch.full((E + 2, n), 0xA5, dtype=torch.uint8, device=DEV) for n in ns]
+
+    def canaries_intact():
+        return all(bool((d[0] == 0xA5).all()) and bool((d[E + 1] == 0xA5).all()) for d in dst)
+
+    passes = [lut]
+    if chunk == 512:
+        passes.append(torch.from_numpy(rng.integers(0, 256, tuple(lut.shape), dtype=np.uint8)).to(DEV))
+    for table in passes:
+        codec.decode_rows(todo, dst_row, cache_row, bad, dst, table, chunk=chunk)
+        torch.cuda.synchronize()
+        assert canaries_intact()
+        codec.decode_rows(todo, dst_row, cache_row, good, dst, lut, chunk=chunk)
+        torch.cuda.synchronize()
+        assert canaries_intact()
+        for e in range(E):
+            for k in range(2):
+                assert torch.equal(dst[k][e + 1].cpu(), raws[e][k])

@@ -234,3 +234,44 @@ def test_compressed_step_copies_only_the_used_record_words(tmp_path):
         assert trimmed > 0
     finally:
         store.release()
+
+
+def test_corrupt_used_lengths_stay_inside_the_record(tmp_path):
+    """The used length the fused step copies comes from the record's last header word;
+    a corrupt one cannot move the copy outside the record: a huge value copies the whole
+    pitch, a negative one only the header and nibble words, and the staging bytes past
+    the copy keep theirs.  (The decode then clamps the same word to the record.)"""
+    from vllm_expert_pager import codec, synthetic
+    from vllm_expert_pager.pager import PARAMS
+
+    experts = synthetic.fp8_experts_device(E, DEV, seed=9)
+    store, pager = build(tmp_path, "c", True, 32, experts)  # expert e in RAM row e
+    try:
+        huge, neg = 4, 5
+        for n in PARAMS:
+            G = store.row_bytes[n] // codec.GROUP
+            store.pinned[n][huge][G] = 2**31 - 1
+            store.pinned[n][neg][G] = -5
+        for t in pager.decode_staging:
+            t.fill_(0xAB)
+        ids = torch.arange(S, dtype=torch.int32, device=DEV).view(1, -1) + 3  # experts 3..10
+        pager.decode(ids)
+        torch.cuda.synchronize()
+        todo = pager.acquire._vram_todo[:S].cpu().tolist()
+        seen = set()
+        for k, n in enumerate(PARAMS):
+            N, P = store.row_bytes[n], store.pitch[n]
+            G = N // codec.GROUP
+            for j, e in enumerate(todo):
+                if e not in (huge, neg):
+                    continue
+                seen.add(e)
+                rec = store.pinned[n][e].view(torch.uint8)
+                used = P if e == huge else 4 * (G + 1 + N // 8)
+                stg = pager.decode_staging[k][j].cpu()
+                assert torch.equal(stg[:used], rec[:used]), (n, e)
+                assert bool((stg[used:] == 0xAB).all()), (n, e)
+        assert seen == {huge, neg}
+        assert pager.step_errors() == 0
+    finally:
+        store.release()
